@@ -1,0 +1,374 @@
+"""Pop-KV decode-time retrieval benchmark (B200).
+
+Workload: Llama-3.1-8B attention shapes -- 32 query / 8 KV
+heads, head_dim 128, bf16 K/V cache at 32768 tokens, group 32, budget 4096 --
+over 32 layer copies (so every step touches far more than the 126 MB L2), each
+decode step appending one token per layer (open-group re-pack) and scoring a
+fresh synthetic query.  One step = score -> select -> fused gather+attention ->
+append for all 32 layers, replayed as one CUDA graph.
+
+Multi-GPU (torchrun, one rank per GPU): weak scaling by KV head -- the job holds
+N sequences, rank r owns KV heads [r*8/N, (r+1)*8/N) of all of them (so per-GPU
+bytes stay those of one 8-head sequence) and all-gathers every layer's attention
+output over NCCL.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  --impl reference times the reference's own CPU
+path (the readable reconstruction scorer + torch.topk + gather + SDPA, restated
+in oracle/reconstruction.py) on the host cores, one layer-step per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT / "fier-2bits_b200", ROOT / "oracle"):
+    sys.path.insert(0, str(p))
+
+import torch  # noqa: E402
+
+METRIC = "retrieval ms/decode-step per layer (score+topk+gather+attn) and HBM GB/s vs peak"
+KVH, QH, D = 8, 32, 128
+PACKED_BYTES = 48  # per token per KV head at D = 128
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--context", type=int, default=32768)
+    ap.add_argument("--budget", type=int, default=4096)
+    ap.add_argument("--cpu-sample-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU paths
+def cpu_layer_step(L: int, budget: int, seed: int):
+    """Inputs for one layer-step of the reference CPU path (fp32, configs[1] shapes)."""
+    from synthetic import SyntheticLayer
+    syn = SyntheticLayer(kv_heads=KVH, q_heads=QH, head_dim=D, seed=seed)
+    k, v = syn.keys_values(L + 1)
+    k, v = k[0].bfloat16().float(), v[0].bfloat16().float()
+    q = syn.queries(L)[0].bfloat16().float()
+    return q, k, v
+
+
+def time_cpu_reference(L: int, budget: int, steps: int, warmup: int):
+    """ms per layer-step of the reference's readable CPU path on all host threads."""
+    import reconstruction as R
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, k, v = cpu_layer_step(L, budget, seed=123)
+    h2k = torch.arange(QH) // (QH // KVH)
+    prefix_k, prefix_v = k[:, :L].contiguous(), v[:, :L].contiguous()
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        R.decode_step(q, prefix_k, prefix_v, k[:, L], v[:, L], head_to_kv=h2k, budget=budget)
+        if i >= warmup:
+            times.append((time.perf_counter() - t0) * 1e3)
+    return sum(times) / len(times), torch.get_num_threads()
+
+
+# -------------------------------------------------------------- GPU run
+def algorithmic_bytes(L, budget, B, kvh, qh, union_rows):
+    score = B * kvh * L * PACKED_BYTES + B * qh * D * 2 + B * qh * L * 4
+    select = B * qh * L * 4 + B * qh * budget * 4
+    attn = 2 * D * 2 * union_rows + B * qh * budget * 4 + 2 * B * qh * D * 2
+    append = B * kvh * (32 * D * 2 + 32 * PACKED_BYTES)  # worst case: a full open group
+    return {"score": score, "select": select, "attention": attn, "append": append}
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    import popkv
+    import popkv_cuda as pk
+    from synthetic import SyntheticLayer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+        group = dist.group.WORLD
+    layers, L0, budget = args.layers, args.context, args.budget
+    B = world  # weak scaling: one sequence per GPU, sharded by KV head
+    total_steps = args.warmup + args.steps + 2
+    stack = popkv.RetrievalStack(layers=layers, batch=B, kv_heads=KVH, q_heads=QH, head_dim=D,
+                                 max_tokens=L0 + total_steps + 1, budget=budget,
+                                 dtype=torch.bfloat16, device=dev, process_group=group)
+    (k0, k1), (q0, q1) = stack.kv_range, stack.q_range
+    gens = []
+    for i in range(layers):
+        syn = SyntheticLayer(kv_heads=KVH, q_heads=QH, head_dim=D, seed=1000 + i, batch=B, device=dev)
+        k, v = syn.keys_values(L0)
+        stack.prefill(i, k[:, k0:k1].bfloat16(), v[:, k0:k1].bfloat16())
+        gens.append(syn)
+        del k, v
+    stack.set_length(L0)
+    # Per-step inputs, generated up front (device pool for the kernel-only timing).
+    qs, ks, vs = [], [], []
+    for s in range(total_steps):
+        q_l, k_l, v_l = [], [], []
+        for i in range(layers):
+            syn = gens[i]
+            q_l.append(syn.queries(L0 + s)[:, q0:q1].bfloat16())
+            kn, vn = syn.keys_values(1, start=L0 + s)
+            k_l.append(kn[:, k0:k1, 0].bfloat16())
+            v_l.append(vn[:, k0:k1, 0].bfloat16())
+        qs.append(torch.stack(q_l)); ks.append(torch.stack(k_l)); vs.append(torch.stack(v_l))
+    torch.cuda.synchronize()
+
+    # Warm-up (eager first step, then graph capture, then graph replays).
+    stack.step(qs[0], ks[0], vs[0])
+    stack.capture()
+    step_idx = 1
+    for _ in range(max(args.warmup - 1, 0)):
+        stack.step(qs[step_idx], ks[step_idx], vs[step_idx]); step_idx += 1
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- timed region: K graph-replayed decode steps, inputs resident in HBM.
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(); torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            stack.step(qs[step_idx], ks[step_idx], vs[step_idx]); step_idx += 1
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = torch.tensor([start.elapsed_time(end)], device=dev)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    ms_step = float(elapsed) / args.steps
+    ms_layer = ms_step / layers
+
+    # ---- per-stage timing (idempotent re-runs of each stage over all layers, no advance).
+    stage_ms = {}
+    reps = 3
+    tokens = stack.max_tokens
+
+    def run_stage(name, i):
+        if name == "score":
+            pk.score(stack.q_in[i], stack.packed[i], head_to_kv=stack.head_to_kv, tokens=tokens,
+                     seq_len=stack.seq_len, out=stack.scores)
+        elif name == "select":
+            pk.select(stack.scores.view(-1, stack.capacity), budget=budget, tokens=tokens,
+                      seq_len=stack.seq_len, rows_per_seq=stack.q_heads, out=stack.indices[i])
+        elif name == "attention":
+            pk.sparse_attention(stack.q_in[i], stack.key_cache[i], stack.value_cache[i],
+                                stack.indices[i], budget=budget, tokens=tokens,
+                                current_keys=stack.k_in[i], current_values=stack.v_in[i],
+                                seq_len=stack.seq_len, workspace=stack.workspace[i], out=stack.out[i])
+        elif name == "append":
+            pk.append_keys(stack.key_cache[i], stack.value_cache[i], stack.k_in[i], stack.v_in[i],
+                           stack.packed[i], position=0, seq_len=stack.seq_len,
+                           kv_heads_per_seq=stack.kv_heads)
+
+    for name in ("score", "select", "attention", "append"):
+        for i in range(layers):
+            run_stage(name, i)  # warm
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            for i in range(layers):
+                if name == "select":
+                    run_stage("score", i)  # select needs this layer's scores
+                run_stage(name, i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        stage_ms[name] = a.elapsed_time(b) / (reps * layers)
+    stage_ms["select"] -= stage_ms["score"]
+
+    # Union of selections per (sequence, KV head) -> attention's algorithmic bytes.
+    L_now = stack.length
+    union_rows = 0
+    for i in range(layers):
+        idx = stack.indices[i].view(B, stack.q_heads, budget).cpu()
+        G = stack.q_heads // stack.kv_heads
+        for b in range(B):
+            for h in range(stack.kv_heads):
+                sel = idx[b, h * G:(h + 1) * G]
+                union_rows += int(torch.unique(sel[sel >= 0]).numel())
+    union_rows //= layers
+    nbytes = algorithmic_bytes(L_now, budget, B, stack.kv_heads, stack.q_heads, union_rows)
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    stages = {n: {"ms": stage_ms[n], "bytes": nbytes[n],
+                  "gbs": nbytes[n] / (stage_ms[n] * 1e-3) / 1e9,
+                  "frac": nbytes[n] / (stage_ms[n] * 1e-3) / 1e9 / hbm} for n in stage_ms}
+    dominant = max(("score", "select", "attention"), key=lambda n: stage_ms[n])
+    step_bytes = sum(nbytes[n] for n in ("score", "select", "attention", "append"))
+
+    # ---- e2e: public API with pinned host inputs and outputs, copies inside the region.
+    host_q = [qs[s % total_steps].cpu().pin_memory() for s in range(args.steps)]
+    host_k = [ks[s % total_steps].cpu().pin_memory() for s in range(args.steps)]
+    host_v = [vs[s % total_steps].cpu().pin_memory() for s in range(args.steps)]
+    out_shape = (stack.gathered if world > 1 else stack.out).shape
+    host_out = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+    # Reset lengths so the e2e steps stay inside the reserve.
+    stack.set_length(L0)
+    torch.cuda.synchronize(); barrier()
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        res = stack.step(host_q[s].to(dev, non_blocking=True), host_k[s].to(dev, non_blocking=True),
+                         host_v[s].to(dev, non_blocking=True))
+        host_out.copy_(res, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([(time.perf_counter() - t0) * 1e3], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_layer = float(e2e_ms) / (args.steps * layers)
+    h2d = host_q[0].nbytes + host_k[0].nbytes + host_v[0].nbytes
+    d2h = host_out.nbytes
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_ms, cores = time_cpu_reference(L0, budget, args.cpu_sample_steps, 1)
+        cpu_baseline = {"value": cpu_ms, "unit": "ms", "cores": cores, "kind": "port",
+                        "sample": f"{args.cpu_sample_steps} layer-steps of configs[1] shapes "
+                                  f"(L={L0}, budget={budget}, fp32 upcast of bf16), after 1 warm-up"}
+
+    if rank == 0:
+        dom = stages[dominant]
+        line = {
+            "metric": METRIC, "value": ms_layer, "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V/Q, 4 outlier channels x8, RoPE 5e5)",
+            "config": {"workload": "configs[1]: Llama-3.1-8B attention layer, 32 q / 8 kv heads, "
+                                   "head_dim 128, bf16 cache, group 32, one append per step",
+                       "context": L0, "budget": budget, "layers_per_step": layers,
+                       "sequences": B, "parallelism": f"kv-head shards x{world}" if world > 1 else "none",
+                       "l2": "inputs larger than L2 (32 layers rotate through ~4.7 GB per GPU)",
+                       "graph": "one CUDA graph per decode step"},
+            "hbm_gbs_step": step_bytes / (ms_layer * 1e-3) / 1e9,
+            "stages": stages,
+            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": dom["gbs"],
+                         "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": dom["frac"],
+                         "traffic": None, "algorithmic_bytes": dom["bytes"],
+                         "union_rows_per_layer": union_rows},
+            "clocks": clocks.summary(),
+            "e2e": {"value": e2e_layer, "unit": "ms", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": stack.launches_per_step() * args.steps,
+            "cpu_baseline": cpu_baseline,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    L, budget = args.context, args.budget
+    ms, cores = time_cpu_reference(L, budget, args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": ms, "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) K/V/Q, 4 outlier channels x8, RoPE 5e5)",
+        "config": {"workload": "configs[1] shapes, one layer-step per step on the host CPU "
+                               "(reference readable reconstruction + torch.topk + gather + SDPA)",
+                   "context": L, "budget": budget},
+        "cpu_baseline": {"value": ms, "unit": "ms", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} layer-steps (L={L}, budget={budget})"},
+        "e2e": {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

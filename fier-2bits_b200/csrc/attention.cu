@@ -1,0 +1,757 @@
+// (f) Fused gather + exact split-K decode attention over the selected tokens.
+//
+// Semantics: for every query head, softmax(q . K_sel^T / sqrt(D)) . V_sel over the
+// head's selected tokens, the newest token (index L) read from the current k/v
+// rows -- the reference's gather_selected_kv + selected_attention
+// (popkv.py:341-368) -- without materialising the gathered rows.
+//
+// B200 layout of the work:
+//  * a scatter kernel turns the [rows, budget] index lists into a per-token bitmask
+//    of the query heads (of one KV head) that selected the token;
+//  * one CTA per (sequence, KV head, token segment) reads the segment's bitmask
+//    (and clears it for the next call), compacts the UNION of its G query heads'
+//    selections, and streams those K/V rows once from HBM with 16-byte cp.async
+//    copies into a per-warp double-buffered shared-memory ring; the G heads share
+//    every row read (GQA);
+//  * each warp runs a flash-decoding tile of 16 rows on the tensor cores
+//    (mma.m16n8k16, bf16/fp16 in, fp32 accumulate) with the query heads packed
+//    into the M dimension, masking every (head, row) pair the head did not select;
+//  * partial (max, sum, acc) per (head, segment) go to the workspace and the last
+//    CTA of a (sequence, KV head) -- found with an atomic ticket, no spinning --
+//    combines them and resets its ticket.
+// fp32 caches and head_dim outside {64, 96, 128} take a SIMT variant of the same
+// segment kernel.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace popkv {
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kMaxGroup = 16;
+constexpr int kSegMax = 2048;   // tokens per segment (multiple of 8)
+constexpr int kTileRows = 16;
+constexpr int kStages = 2;
+constexpr int kMaxSplits = 1024;
+
+struct AttnParams {
+    const void* q;
+    const void* kc;
+    const void* vc;
+    const void* cur_k;
+    const void* cur_v;
+    void* out;
+    const int32_t* indices;
+    int64_t index_stride;
+    int64_t budget;
+    uint16_t* masks;       // [B*KVH][mask_stride]
+    int64_t mask_stride;   // multiple of 8
+    float* ws_m;           // [B*QH][S]
+    float* ws_l;           // [B*QH][S]
+    float* ws_acc;         // [B*QH][S][D]
+    uint32_t* tickets;     // [B*KVH]
+    int B, QH, KVH, G, D;
+    int64_t kv_cap;
+    int per_batch;
+    int64_t tokens;
+    const int32_t* seq_len;
+    int S;
+    float sl2;       // 1/sqrt(D) * log2(e)
+    int work_bytes;  // scratch bytes before the token list (SIMT kernel)
+};
+
+__device__ __forceinline__ int64_t seq_length(const AttnParams& p, int b) {
+    int64_t L = p.seq_len ? static_cast<int64_t>(p.seq_len[b]) : p.tokens;
+    return L < p.tokens ? (L < 0 ? 0 : L) : p.tokens;
+}
+
+__device__ __forceinline__ int64_t segment_len(int64_t L, int S) {
+    return ((L + 1 + S - 1) / S + 7) / 8 * 8;
+}
+
+// ------------------------------------------------------------- scatter kernel
+__global__ void scatter_kernel(AttnParams p) {
+    const int row = blockIdx.y;  // b*QH + qh
+    const int b = row / p.QH;
+    const int qh = row - b * p.QH;
+    const int kvh = qh / p.G;
+    const int bit = qh - kvh * p.G;
+    const int64_t L = seq_length(p, b);
+    const int64_t count = (p.budget - 1 < L ? p.budget - 1 : L) + 1;
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= count) return;
+    const int64_t t = p.indices[row * p.index_stride + j];
+    if (t < 0 || t > L) return;
+    uint32_t* words = reinterpret_cast<uint32_t*>(p.masks + (static_cast<int64_t>(b) * p.KVH + kvh) * p.mask_stride);
+    atomicOr(words + (t >> 1), (1u << bit) << ((t & 1) * 16));
+}
+
+// ------------------------------------------------------ union of one segment
+// Reads the bitmask of tokens [lo, lo+n) (n <= kSegMax, lo multiple of 8), clears
+// it, and writes the selected tokens (ascending) and their head masks to shared
+// memory.  Returns the union size (same value in every thread).
+__device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int n, int* s_tok,
+                           uint16_t* s_msk, int* s_scan, bool dense) {
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    if (dense) {
+        const uint16_t full = static_cast<uint16_t>((1u << p.G) - 1u);
+        for (int i = tid; i < n; i += kAttnThreads) {
+            s_tok[i] = static_cast<int>(lo + i);
+            s_msk[i] = full;
+        }
+        __syncthreads();
+        return n;
+    }
+    constexpr int PER = kSegMax / kAttnThreads;  // 16 tokens = two 16-byte words
+    uint16_t* mrow = p.masks + (static_cast<int64_t>(b) * p.KVH + kvh) * p.mask_stride + lo;
+    const int first = tid * PER;
+    uint16_t m[PER];
+    if (first + PER <= n) {
+        const uint4 w0 = *reinterpret_cast<const uint4*>(mrow + first);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(mrow + first + 8);
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            m[2 * j] = static_cast<uint16_t>(ws[j] & 0xffffu);
+            m[2 * j + 1] = static_cast<uint16_t>(ws[j] >> 16);
+        }
+        if ((w0.x | w0.y | w0.z | w0.w | w1.x | w1.y | w1.z | w1.w) != 0u) {
+            *reinterpret_cast<uint4*>(mrow + first) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(mrow + first + 8) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            m[j] = (first + j < n) ? mrow[first + j] : static_cast<uint16_t>(0);
+            if (m[j]) mrow[first + j] = 0;
+        }
+    }
+    int cnt = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) cnt += m[j] != 0;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_scan[warp] = incl;
+    __syncthreads();
+    int base = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+        base += (w < warp) ? s_scan[w] : 0;
+        total += s_scan[w];
+    }
+    int pos = base + incl - cnt;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        if (m[j]) {
+            s_tok[pos] = static_cast<int>(lo + first + j);
+            s_msk[pos] = m[j];
+            ++pos;
+        }
+    }
+    __syncthreads();
+    return total;
+}
+
+// -------------------------------------------------- completion and combine
+// Called by every thread after this CTA's partials are stored.  The last CTA of
+// (b, kvh) merges the S partials of its G heads into the output.
+template <typename T>
+__device__ void finish_and_combine(const AttnParams& p, int b, int kvh, float* s_w, float* s_l) {
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(p.tickets + b * p.KVH + kvh, 1u);
+        s_last = prev == static_cast<uint32_t>(p.S - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int S = p.S;
+    const int64_t row0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
+    for (int i = threadIdx.x; i < p.G * S; i += blockDim.x) {
+        s_w[i] = __ldcg(p.ws_m + row0 * S + i);
+        s_l[i] = __ldcg(p.ws_l + row0 * S + i);
+    }
+    __syncthreads();
+    for (int h = threadIdx.x; h < p.G; h += blockDim.x) {
+        float M = -INFINITY;
+        for (int s = 0; s < S; ++s) M = fmaxf(M, s_w[h * S + s]);
+        float lsum = 0.0f;
+        for (int s = 0; s < S; ++s) {
+            const float m = s_w[h * S + s];
+            const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
+            s_w[h * S + s] = w;
+            lsum += w * s_l[h * S + s];
+        }
+        s_l[h * S] = 1.0f / lsum;  // s_l row h, slot 0 now holds 1/L
+    }
+    __syncthreads();
+    T* out = static_cast<T*>(p.out);
+    for (int i = threadIdx.x; i < p.G * p.D; i += blockDim.x) {
+        const int h = i / p.D;
+        const int d = i - h * p.D;
+        const float* acc = p.ws_acc + (row0 + h) * S * p.D + d;
+        float o = 0.0f;
+        for (int s = 0; s < S; ++s) {
+            const float w = s_w[h * S + s];
+            if (w != 0.0f) o += w * __ldcg(acc + static_cast<int64_t>(s) * p.D);
+        }
+        out[(row0 + h) * p.D + d] = from_float<T>(o * s_l[h * S]);
+    }
+    if (threadIdx.x == 0) p.tickets[b * p.KVH + kvh] = 0u;
+}
+
+// -------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
+                 "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* smem) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* smem) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+
+template <typename T> struct MmaOp;
+template <> struct MmaOp<__nv_bfloat16> {
+    static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+    static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    }
+};
+template <> struct MmaOp<__half> {
+    static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+    static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+        const __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    }
+};
+
+// Shared-memory plan of the tensor-core kernel (bytes).
+template <typename T, int D>
+struct MmaPlan {
+    static constexpr int LDS = D + 8;  // padded row: conflict-free ldmatrix
+    static constexpr int kStageBytes = 2 * kTileRows * LDS * (int)sizeof(T);
+    static constexpr int kRingBytes = kAttnWarps * kStages * kStageBytes;
+    static constexpr int kMergeBytes = kAttnWarps * kMaxGroup * (D + 2) * 4;
+    static constexpr int kWorkBytes = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
+    static constexpr int kListBytes = kSegMax * 4 + kSegMax * 2;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnParams p) {
+    using Plan = MmaPlan<T, D>;
+    constexpr int LDS = Plan::LDS;
+    constexpr int NT8 = D / 8;   // output n-tiles
+    constexpr int KS = D / 16;   // k-steps of QK
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* work = smem;
+    int* s_tok = reinterpret_cast<int*>(smem + Plan::kWorkBytes);
+    uint16_t* s_msk = reinterpret_cast<uint16_t*>(s_tok + kSegMax);
+    __shared__ int s_scan[kAttnWarps];
+
+    const int s = blockIdx.x;
+    const int b = blockIdx.y / p.KVH;
+    const int kvh = blockIdx.y - b * p.KVH;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int g = lane >> 2;
+    const int tig = lane & 3;
+    const int64_t L = seq_length(p, b);
+    const int64_t seg = segment_len(L, p.S);
+    const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
+    const int64_t hi = imin64(lo + seg, L + 1);
+    const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
+                                    p.indices == nullptr);
+
+    const T* q = static_cast<const T*>(p.q);
+    const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
+    // Query fragments (A operand, heads g and g+8).
+    uint32_t qa[KS][4];
+    {
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(q + (qrow0 + g) * D);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(q + (qrow0 + g + 8) * D);
+        const bool h0 = g < p.G, h1 = g + 8 < p.G;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int c = (16 * kk + 2 * tig) / 2;
+            qa[kk][0] = h0 ? __ldg(q0 + c) : 0u;
+            qa[kk][1] = h1 ? __ldg(q1 + c) : 0u;
+            qa[kk][2] = h0 ? __ldg(q0 + c + 4) : 0u;
+            qa[kk][3] = h1 ? __ldg(q1 + c + 4) : 0u;
+        }
+    }
+
+    const T* kc = static_cast<const T*>(p.kc);
+    const T* vc = static_cast<const T*>(p.vc);
+    const T* cur_k = static_cast<const T*>(p.cur_k);
+    const T* cur_v = static_cast<const T*>(p.cur_v);
+    const int64_t cache_head = (p.per_batch ? static_cast<int64_t>(b) * p.KVH : 0) + kvh;
+    const int64_t cur_row = (static_cast<int64_t>(b) * p.KVH + kvh) * D;
+    T* ring = reinterpret_cast<T*>(work) + warp * kStages * 2 * kTileRows * LDS;
+
+    auto issue = [&](int tile, int st) {
+        T* kd = ring + st * 2 * kTileRows * LDS;
+        T* vd = kd + kTileRows * LDS;
+        constexpr int CPR = D * (int)sizeof(T) / 16;
+        constexpr int EPC = 16 / (int)sizeof(T);
+#pragma unroll
+        for (int c = lane; c < kTileRows * CPR; c += 32) {
+            const int r = c / CPR;
+            const int ch = c - r * CPR;
+            const int e = tile * kTileRows + r;
+            const T* ks = kc;
+            const T* vs = vc;
+            int bytes = 0;
+            if (e < n_union) {
+                const int64_t t = s_tok[e];
+                bytes = 16;
+                if (t == L && cur_k != nullptr) {
+                    ks = cur_k + cur_row;
+                    vs = cur_v + cur_row;
+                } else {
+                    ks = kc + (cache_head * p.kv_cap + t) * D;
+                    vs = vc + (cache_head * p.kv_cap + t) * D;
+                }
+                ks += ch * EPC;
+                vs += ch * EPC;
+            }
+            cp_async16(kd + r * LDS + ch * EPC, ks, bytes);
+            cp_async16(vd + r * LDS + ch * EPC, vs, bytes);
+        }
+    };
+
+    float acc[NT8][4];
+#pragma unroll
+    for (int i = 0; i < NT8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY};
+    float l_run[2] = {0.0f, 0.0f};
+
+    const int n_tiles = (n_union + kTileRows - 1) / kTileRows;
+    const int my_tiles = n_tiles > warp ? (n_tiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
+#pragma unroll
+    for (int st = 0; st < kStages - 1; ++st) {
+        if (st < my_tiles) issue(warp + kAttnWarps * st, st);
+        cp_async_commit();
+    }
+    for (int i = 0; i < my_tiles; ++i) {
+        const int nxt = i + kStages - 1;
+        if (nxt < my_tiles) issue(warp + kAttnWarps * nxt, nxt % kStages);
+        cp_async_commit();
+        cp_async_wait<kStages - 1>();
+        __syncwarp();
+        const int tile = warp + kAttnWarps * i;
+        const T* Ks = ring + (i % kStages) * 2 * kTileRows * LDS;
+        const T* Vs = Ks + kTileRows * LDS;
+
+        // S = Q K^T for the tile's 16 rows (two n-tiles of 8 rows).
+        float sc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+            for (int k2 = 0; k2 < D / 32; ++k2) {
+                uint32_t bf[4];
+                ldmatrix_x4(bf, Ks + (nt * 8 + (lane & 7)) * LDS + k2 * 32 + (lane >> 3) * 8);
+                MmaOp<T>::run(sc[nt], qa[2 * k2], bf[0], bf[1]);
+                MmaOp<T>::run(sc[nt], qa[2 * k2 + 1], bf[2], bf[3]);
+            }
+        }
+        // Mask (head not selecting the row, or padding row) and scale to log2 domain.
+        float x[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int e = tile * kTileRows + nt * 8 + 2 * tig + j;
+                const uint32_t mk = e < n_union ? s_msk[e] : 0u;
+                x[nt][j] = ((mk >> g) & 1u) ? sc[nt][j] * p.sl2 : -INFINITY;
+                x[nt][2 + j] = ((mk >> (g + 8)) & 1u) ? sc[nt][2 + j] * p.sl2 : -INFINITY;
+            }
+        }
+        float pr[2][4];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            float tmax = fmaxf(fmaxf(x[0][2 * hh], x[0][2 * hh + 1]), fmaxf(x[1][2 * hh], x[1][2 * hh + 1]));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+            const float m_new = fmaxf(m_run[hh], tmax);
+            const bool none = m_new == -INFINITY;
+            const float corr = none ? 1.0f : exp2f(m_run[hh] - m_new);
+            float psum = 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float v = x[nt][2 * hh + j];
+                    const float e = (v == -INFINITY) ? 0.0f : exp2f(v - m_new);
+                    pr[nt][2 * hh + j] = e;
+                    psum += e;
+                }
+            }
+            l_run[hh] = l_run[hh] * corr + psum;
+            m_run[hh] = m_new;
+#pragma unroll
+            for (int n8 = 0; n8 < NT8; ++n8) {
+                acc[n8][2 * hh] *= corr;
+                acc[n8][2 * hh + 1] *= corr;
+            }
+        }
+        uint32_t pa[4];
+        pa[0] = MmaOp<T>::pack(pr[0][0], pr[0][1]);
+        pa[1] = MmaOp<T>::pack(pr[0][2], pr[0][3]);
+        pa[2] = MmaOp<T>::pack(pr[1][0], pr[1][1]);
+        pa[3] = MmaOp<T>::pack(pr[1][2], pr[1][3]);
+        // O += P V.
+#pragma unroll
+        for (int np = 0; np < D / 16; ++np) {
+            uint32_t bf[4];
+            ldmatrix_x4_trans(bf, Vs + (((lane >> 3) & 1) * 8 + (lane & 7)) * LDS + np * 16 + (lane >> 4) * 8);
+            MmaOp<T>::run(acc[2 * np], pa, bf[0], bf[1]);
+            MmaOp<T>::run(acc[2 * np + 1], pa, bf[2], bf[3]);
+        }
+        __syncwarp();
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 1);
+        l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 2);
+    }
+    __syncthreads();  // ring no longer needed: reuse it for the warp merge
+    float* s_wm = reinterpret_cast<float*>(work);            // [warps][16]
+    float* s_wl = s_wm + kAttnWarps * kMaxGroup;              // [warps][16]
+    float* s_wacc = s_wl + kAttnWarps * kMaxGroup;            // [warps][16][D]
+    if (tig == 0) {
+        s_wm[warp * kMaxGroup + g] = m_run[0];
+        s_wm[warp * kMaxGroup + g + 8] = m_run[1];
+        s_wl[warp * kMaxGroup + g] = l_run[0];
+        s_wl[warp * kMaxGroup + g + 8] = l_run[1];
+    }
+#pragma unroll
+    for (int n8 = 0; n8 < NT8; ++n8) {
+        const int c = n8 * 8 + 2 * tig;
+        float* r0 = s_wacc + (warp * kMaxGroup + g) * D + c;
+        float* r1 = s_wacc + (warp * kMaxGroup + g + 8) * D + c;
+        r0[0] = acc[n8][0];
+        r0[1] = acc[n8][1];
+        r1[0] = acc[n8][2];
+        r1[1] = acc[n8][3];
+    }
+    __syncthreads();
+    for (int i = tid; i < p.G * D; i += kAttnThreads) {
+        const int h = i / D;
+        const int d = i - h * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_wm[w * kMaxGroup + h]);
+        float a = 0.0f, l = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float mw = s_wm[w * kMaxGroup + h];
+                const float f = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+                a += f * s_wacc[(w * kMaxGroup + h) * D + d];
+                l += f * s_wl[w * kMaxGroup + h];
+            }
+        }
+        const int64_t prow = (qrow0 + h) * p.S + s;
+        p.ws_acc[prow * D + d] = a;
+        if (d == 0) {
+            p.ws_m[prow] = M;
+            p.ws_l[prow] = l;
+        }
+    }
+    __syncthreads();
+    finish_and_combine<T>(p, b, kvh, reinterpret_cast<float*>(work),
+                          reinterpret_cast<float*>(work) + kMaxGroup * p.S);
+}
+
+// SIMT variant (fp32 caches, or head_dim outside the tensor-core instances).
+template <typename T>
+__global__ void __launch_bounds__(kAttnThreads) attention_simt_kernel(AttnParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    // [0, work_bytes): merge / combine scratch; then token list and masks.
+    int* s_tok = reinterpret_cast<int*>(smem + p.work_bytes);
+    uint16_t* s_msk = reinterpret_cast<uint16_t*>(s_tok + kSegMax);
+    __shared__ int s_scan[kAttnWarps];
+    float* s_wm = reinterpret_cast<float*>(smem);
+    float* s_wl = s_wm + kAttnWarps;
+    float* s_wacc = s_wl + kAttnWarps;  // [warps][D]
+
+    const int s = blockIdx.x;
+    const int b = blockIdx.y / p.KVH;
+    const int kvh = blockIdx.y - b * p.KVH;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int D = p.D;
+    const int64_t L = seq_length(p, b);
+    const int64_t seg = segment_len(L, p.S);
+    const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
+    const int64_t hi = imin64(lo + seg, L + 1);
+    const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
+                                    p.indices == nullptr);
+    const T* q = static_cast<const T*>(p.q);
+    const T* kc = static_cast<const T*>(p.kc);
+    const T* vc = static_cast<const T*>(p.vc);
+    const T* cur_k = static_cast<const T*>(p.cur_k);
+    const T* cur_v = static_cast<const T*>(p.cur_v);
+    const int64_t cache_head = (p.per_batch ? static_cast<int64_t>(b) * p.KVH : 0) + kvh;
+    const int64_t cur_row = (static_cast<int64_t>(b) * p.KVH + kvh) * D;
+    const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
+    const float sl2 = p.sl2;
+
+    for (int h = 0; h < p.G; ++h) {
+        float qv[8], av[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = lane + 32 * j;
+            qv[j] = c < D ? to_float<T>(q[(qrow0 + h) * D + c]) : 0.0f;
+            av[j] = 0.0f;
+        }
+        float m_run = -INFINITY, l_run = 0.0f;
+        for (int e = warp; e < n_union; e += kAttnWarps) {
+            if (!((s_msk[e] >> h) & 1u)) continue;
+            const int64_t t = s_tok[e];
+            const T* kr = (t == L && cur_k) ? cur_k + cur_row : kc + (cache_head * p.kv_cap + t) * D;
+            const T* vr = (t == L && cur_v) ? cur_v + cur_row : vc + (cache_head * p.kv_cap + t) * D;
+            float dot = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = lane + 32 * j;
+                if (c < D) dot += qv[j] * to_float<T>(kr[c]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            const float xv = dot * sl2;
+            const float m_new = fmaxf(m_run, xv);
+            const float corr = exp2f(m_run - m_new);
+            const float pe = exp2f(xv - m_new);
+            l_run = l_run * corr + pe;
+            m_run = m_new;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = lane + 32 * j;
+                av[j] = av[j] * corr + (c < D ? pe * to_float<T>(vr[c]) : 0.0f);
+            }
+        }
+        if (lane == 0) {
+            s_wm[warp] = m_run;
+            s_wl[warp] = l_run;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = lane + 32 * j;
+            if (c < D) s_wacc[warp * D + c] = av[j];
+        }
+        __syncthreads();
+        for (int d = tid; d < D; d += kAttnThreads) {
+            float M = -INFINITY;
+            for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, s_wm[w]);
+            float a = 0.0f, l = 0.0f;
+            if (M != -INFINITY) {
+                for (int w = 0; w < kAttnWarps; ++w) {
+                    const float f = (s_wm[w] == -INFINITY) ? 0.0f : exp2f(s_wm[w] - M);
+                    a += f * s_wacc[w * D + d];
+                    l += f * s_wl[w];
+                }
+            }
+            const int64_t prow = (qrow0 + h) * p.S + s;
+            p.ws_acc[prow * D + d] = a;
+            if (d == 0) {
+                p.ws_m[prow] = M;
+                p.ws_l[prow] = l;
+            }
+        }
+        __syncthreads();
+    }
+    finish_and_combine<T>(p, b, kvh, reinterpret_cast<float*>(smem),
+                          reinterpret_cast<float*>(smem) + kMaxGroup * p.S);
+}
+
+struct WorkspaceLayout {
+    size_t tickets, masks, m, l, acc, total;
+    int64_t mask_stride;
+};
+
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+WorkspaceLayout layout(int64_t B, int64_t QH, int64_t KVH, int64_t D, int64_t tokens, int64_t S) {
+    WorkspaceLayout w;
+    w.mask_stride = (tokens + 1 + 7) / 8 * 8;
+    w.tickets = 0;
+    w.masks = w.tickets + align256(sizeof(uint32_t) * B * KVH);
+    w.m = w.masks + align256(sizeof(uint16_t) * B * KVH * w.mask_stride);
+    w.l = w.m + align256(sizeof(float) * B * QH * S);
+    w.acc = w.l + align256(sizeof(float) * B * QH * S);
+    w.total = w.acc + align256(sizeof(float) * B * QH * S * D);
+    return w;
+}
+
+int64_t auto_splits(int64_t B, int64_t KVH, int64_t tokens) {
+    const int64_t min_s = (tokens + 1 + (kSegMax - 8) - 1) / (kSegMax - 8);
+    const int64_t fill = (2 * 148 + B * KVH - 1) / (B * KVH);
+    int64_t S = min_s > fill ? min_s : fill;
+    const int64_t max_useful = (tokens + 1 + 63) / 64;  // keep >= 64 tokens per segment
+    if (S > max_useful && max_useful >= min_s) S = max_useful;
+    if (S < 1) S = 1;
+    return S;
+}
+
+template <typename T, int D>
+int launch_mma(const AttnParams& p, cudaStream_t st) {
+    using Plan = MmaPlan<T, D>;
+    // The combine scratch (2 x 16 x S floats) reuses the copy ring.
+    const size_t combine = (size_t)2 * kMaxGroup * p.S * 4;
+    const size_t smem = (Plan::kWorkBytes > combine ? (size_t)Plan::kWorkBytes : combine) +
+                        Plan::kListBytes;
+    if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
+    auto kern = attention_mma_kernel<T, D>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), kAttnThreads, smem, st>>>(p);
+    return check_launch("popkv_sparse_attention");
+}
+
+template <typename T>
+int launch_simt(AttnParams p, cudaStream_t st) {
+    const int combine = 2 * kMaxGroup * p.S * 4;
+    const int merge = (2 * kAttnWarps + kAttnWarps * p.D) * 4;
+    p.work_bytes = (combine > merge ? combine : merge + 15) / 16 * 16;
+    const size_t smem = (size_t)p.work_bytes + kSegMax * 6;
+    if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
+    auto kern = attention_simt_kernel<T>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), kAttnThreads, smem, st>>>(p);
+    return check_launch("popkv_sparse_attention");
+}
+
+}  // namespace
+}  // namespace popkv
+
+using namespace popkv;
+
+extern "C" size_t popkv_sparse_attention_workspace_bytes(int64_t batch, int64_t q_heads,
+                                                         int64_t kv_heads, int64_t head_dim,
+                                                         int64_t tokens, int64_t splits) {
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || tokens < 0) return 0;
+    const int64_t S = splits > 0 ? splits : auto_splits(batch, kv_heads, tokens);
+    return layout(batch, q_heads, kv_heads, head_dim, tokens, S).total;
+}
+
+extern "C" int popkv_sparse_attention(const void* queries, int dtype, int64_t batch,
+                                      int64_t q_heads, int64_t head_dim, const void* key_cache,
+                                      const void* value_cache, int64_t kv_heads,
+                                      int64_t kv_capacity, int cache_per_batch,
+                                      const void* current_keys, const void* current_values,
+                                      const int32_t* indices, int64_t index_stride,
+                                      int64_t budget, int64_t tokens, const int32_t* seq_len,
+                                      void* out, void* workspace, size_t workspace_bytes,
+                                      int64_t splits, popkv_stream_t stream) {
+    const size_t es = dtype_size(dtype);
+    if (es == 0) return fail(POPKV_ERR_UNSUPPORTED, "dtype %d is not fp32/fp16/bf16", dtype);
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "invalid attention shape");
+    if (q_heads % kv_heads != 0 || q_heads / kv_heads > kMaxGroup)
+        return fail(POPKV_ERR_UNSUPPORTED, "q_heads/kv_heads must be an integer <= %d", kMaxGroup);
+    if (head_dim > 256 || head_dim % 8 != 0)
+        return fail(POPKV_ERR_UNSUPPORTED, "head_dim must be a multiple of 8 and <= 256");
+    if (tokens < 0 || tokens >= kv_capacity + (current_keys ? 1 : 0))
+        return fail(POPKV_ERR_CAPACITY, "tokens %lld do not fit the KV capacity %lld",
+                    (long long)tokens, (long long)kv_capacity);
+    if ((current_keys == nullptr) != (current_values == nullptr))
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "current_keys and current_values go together");
+    if (indices != nullptr && (budget <= 1 || index_stride < budget))
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "indices need budget > 1 and index_stride >= budget");
+    if (!queries || !key_cache || !value_cache || !out || !workspace)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
+    if (!aligned(key_cache, 16) || !aligned(value_cache, 16) || !aligned(queries, 16) ||
+        !aligned(workspace, 256) || (current_keys && (!aligned(current_keys, 16) || !aligned(current_values, 16))))
+        return fail(POPKV_ERR_ALIGNMENT, "caches, queries and current rows need 16-byte alignment, workspace 256");
+    const int64_t S = splits > 0 ? splits : auto_splits(batch, kv_heads, tokens);
+    if (S > kMaxSplits) return fail(POPKV_ERR_UNSUPPORTED, "splits %lld > %d", (long long)S, kMaxSplits);
+    if (((tokens + 1 + S - 1) / S + 7) / 8 * 8 > kSegMax)
+        return fail(POPKV_ERR_UNSUPPORTED, "segment longer than %d tokens: raise splits", kSegMax);
+    if (batch * kv_heads > 65535) return fail(POPKV_ERR_UNSUPPORTED, "too many (batch, kv head) pairs");
+    const WorkspaceLayout w = layout(batch, q_heads, kv_heads, head_dim, tokens, S);
+    if (workspace_bytes < w.total)
+        return fail(POPKV_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", workspace_bytes, w.total);
+
+    AttnParams p;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    p.q = queries; p.kc = key_cache; p.vc = value_cache;
+    p.cur_k = current_keys; p.cur_v = current_values; p.out = out;
+    p.indices = indices; p.index_stride = index_stride; p.budget = budget;
+    p.masks = reinterpret_cast<uint16_t*>(ws + w.masks);
+    p.mask_stride = w.mask_stride;
+    p.ws_m = reinterpret_cast<float*>(ws + w.m);
+    p.ws_l = reinterpret_cast<float*>(ws + w.l);
+    p.ws_acc = reinterpret_cast<float*>(ws + w.acc);
+    p.tickets = reinterpret_cast<uint32_t*>(ws + w.tickets);
+    p.B = (int)batch; p.QH = (int)q_heads; p.KVH = (int)kv_heads;
+    p.G = (int)(q_heads / kv_heads); p.D = (int)head_dim;
+    p.kv_cap = kv_capacity; p.per_batch = cache_per_batch != 0;
+    p.tokens = tokens; p.seq_len = seq_len; p.S = (int)S;
+    p.sl2 = (float)((1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634);
+    p.work_bytes = 0;
+    const cudaStream_t st = as_stream(stream);
+
+    if (indices != nullptr) {
+        const int64_t per_row = (budget < tokens + 1 ? budget : tokens + 1);
+        const dim3 grid((unsigned)((per_row + 255) / 256), (unsigned)(batch * q_heads));
+        scatter_kernel<<<grid, 256, 0, st>>>(p);
+        const int rc = check_launch("popkv_sparse_attention (scatter)");
+        if (rc != POPKV_OK) return rc;
+    }
+    if (dtype == POPKV_BF16) {
+        if (head_dim == 128) return launch_mma<__nv_bfloat16, 128>(p, st);
+        if (head_dim == 64) return launch_mma<__nv_bfloat16, 64>(p, st);
+        if (head_dim == 96) return launch_mma<__nv_bfloat16, 96>(p, st);
+        return launch_simt<__nv_bfloat16>(p, st);
+    }
+    if (dtype == POPKV_F16) {
+        if (head_dim == 128) return launch_mma<__half, 128>(p, st);
+        if (head_dim == 64) return launch_mma<__half, 64>(p, st);
+        if (head_dim == 96) return launch_mma<__half, 96>(p, st);
+        return launch_simt<__half>(p, st);
+    }
+    return launch_simt<float>(p, st);
+}

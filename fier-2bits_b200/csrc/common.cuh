@@ -1,0 +1,85 @@
+// Shared device helpers and host-side error plumbing of the Pop-KV B200 library.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "popkv_b200.h"
+
+namespace popkv {
+
+// ---------------------------------------------------------------- host side
+void set_error(const char* fmt, ...);
+int fail(int status, const char* fmt, ...);
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(popkv_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline size_t dtype_size(int dtype) {
+    switch (dtype) {
+        case POPKV_F32: return 4;
+        case POPKV_F16: return 2;
+        case POPKV_BF16: return 2;
+        default: return 0;
+    }
+}
+
+// --------------------------------------------------------------- device side
+template <typename T> __device__ __forceinline__ float to_float(T v);
+template <> __device__ __forceinline__ float to_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_float<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) {
+    return __bfloat162float(v);
+}
+
+template <typename T> __device__ __forceinline__ T from_float(float v);
+template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+
+// Representative division.  Default: IEEE round-to-nearest.  With reference
+// division the PTX full-range approximate divide is issued instead, which is what
+// a --use_fast_math build (the reference's JIT flags) uses for float '/'.
+__device__ __forceinline__ float rep_div(float a, float b, bool reference_division) {
+    if (reference_division) {
+        float r;
+        asm("div.full.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+        return r;
+    }
+    return __fdiv_rn(a, b);
+}
+
+// Mean of the low / high lanes with the reference's fallbacks
+// (csrc/popkv_ext.cu:77-83 and 139-145).
+__device__ __forceinline__ void representatives(float low_sum, int low_count, float high_sum,
+                                                int high_count, bool ref_div, float& low,
+                                                float& high) {
+    if (low_count == 0) {
+        low = high_count ? rep_div(high_sum, static_cast<float>(high_count), ref_div) : 0.0f;
+        high = low;
+    } else {
+        low = rep_div(low_sum, static_cast<float>(low_count), ref_div);
+        high = high_count ? rep_div(high_sum, static_cast<float>(high_count), ref_div) : low;
+    }
+}
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// Order-preserving map of fp32 to uint32 (larger float -> larger key); -0.0 maps
+// like +0.0 so that the two compare equal, as float comparison does.
+__device__ __forceinline__ uint32_t order_key(float x) {
+    uint32_t u = __float_as_uint(x);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+}  // namespace popkv

@@ -1,0 +1,291 @@
+// (c) Query packer fused with (d) the popcount scorer.
+//
+// Semantics follow popkv_score_kernel (csrc/popkv_ext.cu:93-178): each query row
+// is packed with per-row thresholds max*0.5 / min*0.5, per-word fp32 low/delta
+// representatives summed in channel order; each token's score is the sum over
+// words, in word order, of
+//   fmaf(ql*kl, Cs, fmaf(dq*kl, Cq, fmaf(ql*dk, Ck, dq*dk*Cqk)))
+// with Cs/Cq/Ck/Cqk = 2*popc(match & x) - popc(x), then multiplied by 1/sqrt(D).
+//
+// B200 layout of the work: one CTA per (sequence, KV head, 512-token tile) serves
+// every query head mapped to that KV head, so each packed row (48 B at D = 128)
+// is read from HBM once for the whole GQA group (the reference re-reads it once
+// per query head).  Each thread owns two tokens and fetches their sign/mag words
+// with 16-byte loads and low/delta with 8-byte loads, issued before the query
+// pack so that the HBM latency overlaps it.  The query pack itself is
+// warp-parallel (ballots for the bit words) with the sequential channel-order
+// sums kept on one lane per word.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace popkv {
+namespace {
+
+constexpr int kScoreThreads = 256;
+constexpr int kTokensPerThread = 2;
+constexpr int kTile = kScoreThreads * kTokensPerThread;
+
+template <int W, bool VEC>
+struct PackedRow {
+    uint32_t s[W], m[W];
+    uint16_t l[W], d[W];
+
+    __device__ __forceinline__ void load(const int32_t* __restrict__ sg,
+                                         const int32_t* __restrict__ mg,
+                                         const uint16_t* __restrict__ lo,
+                                         const uint16_t* __restrict__ de, int64_t base) {
+        if constexpr (VEC && W % 4 == 0) {
+#pragma unroll
+            for (int j = 0; j < W; j += 4) {
+                const uint4 a = __ldg(reinterpret_cast<const uint4*>(sg + base + j));
+                const uint4 b = __ldg(reinterpret_cast<const uint4*>(mg + base + j));
+                const uint2 c = __ldg(reinterpret_cast<const uint2*>(lo + base + j));
+                const uint2 e = __ldg(reinterpret_cast<const uint2*>(de + base + j));
+                s[j] = a.x; s[j + 1] = a.y; s[j + 2] = a.z; s[j + 3] = a.w;
+                m[j] = b.x; m[j + 1] = b.y; m[j + 2] = b.z; m[j + 3] = b.w;
+                l[j] = c.x & 0xffffu; l[j + 1] = c.x >> 16; l[j + 2] = c.y & 0xffffu; l[j + 3] = c.y >> 16;
+                d[j] = e.x & 0xffffu; d[j + 1] = e.x >> 16; d[j + 2] = e.y & 0xffffu; d[j + 3] = e.y >> 16;
+            }
+        } else if constexpr (VEC && W % 2 == 0) {
+#pragma unroll
+            for (int j = 0; j < W; j += 2) {
+                const uint2 a = __ldg(reinterpret_cast<const uint2*>(sg + base + j));
+                const uint2 b = __ldg(reinterpret_cast<const uint2*>(mg + base + j));
+                const uint32_t c = __ldg(reinterpret_cast<const unsigned int*>(lo + base + j));
+                const uint32_t e = __ldg(reinterpret_cast<const unsigned int*>(de + base + j));
+                s[j] = a.x; s[j + 1] = a.y; m[j] = b.x; m[j + 1] = b.y;
+                l[j] = c & 0xffffu; l[j + 1] = c >> 16; d[j] = e & 0xffffu; d[j + 1] = e >> 16;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < W; ++j) {
+                s[j] = static_cast<uint32_t>(__ldg(sg + base + j));
+                m[j] = static_cast<uint32_t>(__ldg(mg + base + j));
+                l[j] = __ldg(lo + base + j);
+                d[j] = __ldg(de + base + j);
+            }
+        }
+    }
+};
+
+template <typename TQ, int W, bool VEC>
+__global__ void __launch_bounds__(kScoreThreads)
+score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
+             const int32_t* __restrict__ k_sign, const int32_t* __restrict__ k_mag,
+             const uint16_t* __restrict__ k_low, const uint16_t* __restrict__ k_delta,
+             int kv_heads, int64_t capacity, bool per_batch,
+             const int64_t* __restrict__ head_to_kv, int64_t tokens,
+             const int32_t* __restrict__ seq_len, float* __restrict__ scores, int64_t stride,
+             float scale, bool ref_div) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    int* s_heads = reinterpret_cast<int*>(smem_raw);                 // [q_heads]
+    uint32_t* s_qs = reinterpret_cast<uint32_t*>(s_heads + q_heads);  // [q_heads][W]
+    uint32_t* s_qm = s_qs + q_heads * W;
+    float* s_ql = reinterpret_cast<float*>(s_qm + q_heads * W);
+    float* s_qd = s_ql + q_heads * W;
+    __shared__ int s_nh;
+
+    const int b = blockIdx.y / kv_heads;
+    const int kvh = blockIdx.y - b * kv_heads;
+    int64_t L = seq_len ? static_cast<int64_t>(seq_len[b]) : tokens;
+    L = L < tokens ? L : tokens;
+    const int64_t t_base = static_cast<int64_t>(blockIdx.x) * kTile;
+    if (t_base >= L) return;  // uniform over the CTA
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+
+    // 1. Issue the packed-row loads first.
+    const int64_t cache_head = (per_batch ? static_cast<int64_t>(b) * kv_heads : 0) + kvh;
+    PackedRow<W, VEC> rows[kTokensPerThread];
+#pragma unroll
+    for (int j = 0; j < kTokensPerThread; ++j) {
+        const int64_t t = t_base + j * kScoreThreads + tid;
+        if (t < L) rows[j].load(k_sign, k_mag, k_low, k_delta, (cache_head * capacity + t) * W);
+    }
+
+    // 2. Query heads of this KV head, in ascending head order.
+    if (warp == 0) {
+        int count = 0;
+        for (int q0 = 0; q0 < q_heads; q0 += 32) {
+            const int qh = q0 + lane;
+            const bool mine = qh < q_heads && head_to_kv[qh] == kvh;
+            const unsigned bal = __ballot_sync(0xffffffffu, mine);
+            if (mine) s_heads[count + __popc(bal & ((1u << lane) - 1u))] = qh;
+            count += __popc(bal);
+        }
+        if (lane == 0) s_nh = count;
+    }
+    __syncthreads();
+    const int nh = s_nh;
+
+    // 3. Warp-parallel query pack, one warp per query head.
+    for (int slot = warp; slot < nh; slot += kScoreThreads / 32) {
+        const TQ* q = queries + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * D;
+        float v[W];
+        float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const int c = 32 * j + lane;
+            v[j] = c < D ? to_float<TQ>(q[c]) : 0.0f;
+            if (c < D) { mn = fminf(mn, v[j]); mx = fmaxf(mx, v[j]); }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        const float neg = mn * 0.5f, pos = mx * 0.5f;
+        uint32_t my_sw = 0u, my_mw = 0u;
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const bool valid = 32 * j + lane < D;
+            const bool sg = valid && v[j] >= 0.0f;
+            const bool mg = valid && (sg ? v[j] > pos : v[j] < neg);
+            const uint32_t sw = __ballot_sync(0xffffffffu, sg);
+            const uint32_t mw = __ballot_sync(0xffffffffu, mg);
+            if (lane == j) { my_sw = sw; my_mw = mw; }
+        }
+        // Channel-order sums: lane j accumulates word j.
+        float ls = 0.0f, hs = 0.0f;
+        int lc = 0, hc = 0;
+        for (int i = 0; i < 32; ++i) {
+#pragma unroll
+            for (int j = 0; j < W; ++j) {
+                const float x = __shfl_sync(0xffffffffu, v[j], i);
+                if (lane == j && 32 * j + i < D) {
+                    if ((my_mw >> i) & 1u) { hs += fabsf(x); ++hc; }
+                    else { ls += fabsf(x); ++lc; }
+                }
+            }
+        }
+        if (lane < W) {
+            float low, high;
+            representatives(ls, lc, hs, hc, ref_div, low, high);
+            s_qs[slot * W + lane] = my_sw;
+            s_qm[slot * W + lane] = my_mw;
+            s_ql[slot * W + lane] = low;
+            s_qd[slot * W + lane] = high - low;
+        }
+    }
+    __syncthreads();
+
+    const uint32_t last_valid = (D & 31) ? ((1u << (D & 31)) - 1u) : 0xffffffffu;
+    const float sc = ref_div ? rsqrtf(static_cast<float>(D)) : scale;
+    for (int slot = 0; slot < nh; ++slot) {
+        float* out = scores + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * stride;
+#pragma unroll
+        for (int j = 0; j < kTokensPerThread; ++j) {
+            const int64_t t = t_base + j * kScoreThreads + tid;
+            if (t >= L) continue;
+            float score = 0.0f;
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
+                const uint32_t qs = s_qs[slot * W + w];
+                const uint32_t qm = s_qm[slot * W + w] & valid;
+                const uint32_t km = rows[j].m[w] & valid;
+                const uint32_t match = ~(qs ^ rows[j].s[w]) & valid;
+                const uint32_t both = qm & km;
+                const int cs = 2 * __popc(match) - __popc(valid);
+                const int cq = 2 * __popc(match & qm) - __popc(qm);
+                const int ck = 2 * __popc(match & km) - __popc(km);
+                const int cqk = 2 * __popc(match & both) - __popc(both);
+                const float ql = s_ql[slot * W + w], dq = s_qd[slot * W + w];
+                const float kl = __half2float(__ushort_as_half(rows[j].l[w]));
+                const float dk = __half2float(__ushort_as_half(rows[j].d[w]));
+                const float inner = __fmul_rn(__fmul_rn(dq, dk), static_cast<float>(cqk));
+                const float gs = fmaf(__fmul_rn(ql, kl), static_cast<float>(cs),
+                                      fmaf(__fmul_rn(dq, kl), static_cast<float>(cq),
+                                           fmaf(__fmul_rn(ql, dk), static_cast<float>(ck), inner)));
+                score = __fadd_rn(score, gs);
+            }
+            out[t] = __fmul_rn(score, sc);
+        }
+    }
+}
+
+template <typename TQ, int W>
+int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const int32_t* sg,
+                   const int32_t* mg, const uint16_t* lo, const uint16_t* de, int64_t kv_heads,
+                   int64_t cap, bool per_batch, const int64_t* h2k, int64_t tokens,
+                   const int32_t* seq_len, float* scores, int64_t stride, float scale,
+                   bool ref_div, bool vec, cudaStream_t st) {
+    const dim3 grid((unsigned)((tokens + kTile - 1) / kTile), (unsigned)(batch * kv_heads));
+    const size_t smem = (size_t)q_heads * (sizeof(int) + (size_t)W * 16);
+    auto run = [&](auto kern) {
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, kScoreThreads, smem, st>>>(
+            static_cast<const TQ*>(q), (int)q_heads, D, sg, mg, lo, de, (int)kv_heads, cap,
+            per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div);
+    };
+    if (vec) run(score_kernel<TQ, W, true>);
+    else run(score_kernel<TQ, W, false>);
+    return check_launch("popkv_score");
+}
+
+template <typename TQ, typename... A>
+int score_words(int W, A... a) {
+    switch (W) {
+        case 1: return launch_score_t<TQ, 1>(a...);
+        case 2: return launch_score_t<TQ, 2>(a...);
+        case 3: return launch_score_t<TQ, 3>(a...);
+        case 4: return launch_score_t<TQ, 4>(a...);
+        case 5: return launch_score_t<TQ, 5>(a...);
+        case 6: return launch_score_t<TQ, 6>(a...);
+        case 7: return launch_score_t<TQ, 7>(a...);
+        case 8: return launch_score_t<TQ, 8>(a...);
+        default: return fail(POPKV_ERR_UNSUPPORTED, "head_dim above 256 is not supported");
+    }
+}
+
+}  // namespace
+}  // namespace popkv
+
+using namespace popkv;
+
+extern "C" int popkv_score(const void* queries, int q_dtype, int64_t batch, int64_t q_heads,
+                           int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                           const uint16_t* low, const uint16_t* delta, int64_t kv_heads,
+                           int64_t capacity, int cache_per_batch, const int64_t* head_to_kv,
+                           int64_t tokens, const int32_t* seq_len, float* scores,
+                           int64_t score_stride, int flags, popkv_stream_t stream) {
+    if (dtype_size(q_dtype) == 0)
+        return fail(POPKV_ERR_UNSUPPORTED, "queries dtype %d is not fp32/fp16/bf16", q_dtype);
+    if (batch < 0 || q_heads <= 0 || head_dim <= 0 || kv_heads <= 0)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "queries must be [batch, q_heads, head_dim]");
+    if (head_dim > 256) return fail(POPKV_ERR_UNSUPPORTED, "head_dim %lld > 256", (long long)head_dim);
+    if (tokens <= 0 || tokens > capacity)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "invalid score token count %lld (capacity %lld)",
+                    (long long)tokens, (long long)capacity);
+    if (score_stride < tokens)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "score_stride %lld < tokens %lld",
+                    (long long)score_stride, (long long)tokens);
+    if (q_heads > 4096 || batch * kv_heads > 65535)
+        return fail(POPKV_ERR_UNSUPPORTED, "too many heads for one launch");
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !k_sign || !k_mag || !low || !delta || !head_to_kv || !scores)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
+    const int W = (int)((head_dim + 31) / 32);
+    const bool vec = aligned(k_sign, 16) && aligned(k_mag, 16) && aligned(low, 8) && aligned(delta, 8);
+    const float scale = (float)(1.0 / std::sqrt((double)head_dim));
+    const bool ref_div = (flags & POPKV_FLAG_REFERENCE_DIVISION) != 0;
+    const cudaStream_t st = as_stream(stream);
+    switch (q_dtype) {
+        case POPKV_F32:
+            return score_words<float>(W, queries, batch, q_heads, (int)head_dim, k_sign, k_mag, low,
+                                      delta, kv_heads, capacity, cache_per_batch != 0, head_to_kv,
+                                      tokens, seq_len, scores, score_stride, scale, ref_div, vec, st);
+        case POPKV_F16:
+            return score_words<__half>(W, queries, batch, q_heads, (int)head_dim, k_sign, k_mag, low,
+                                       delta, kv_heads, capacity, cache_per_batch != 0, head_to_kv,
+                                       tokens, seq_len, scores, score_stride, scale, ref_div, vec, st);
+        default:
+            return score_words<__nv_bfloat16>(W, queries, batch, q_heads, (int)head_dim, k_sign,
+                                              k_mag, low, delta, kv_heads, capacity,
+                                              cache_per_batch != 0, head_to_kv, tokens, seq_len,
+                                              scores, score_stride, scale, ref_div, vec, st);
+    }
+}

@@ -1,0 +1,331 @@
+// Thin torch extension over the C ABI (include/popkv_b200.h).
+//
+// Mirrors the reference's pybind surface (csrc/popkv_ext.cpp:12-16: pack,
+// pack_into, score) and adds the rest of the retrieval path (append, select,
+// sparse_attention, advance).  Every function validates with TORCH_CHECK, hands
+// raw device pointers and the current CUDA stream to the C ABI, and turns a
+// non-zero status into a RuntimeError carrying the library's message.  No
+// computation happens here.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "popkv_b200.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_CONTIGUOUS(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_DTYPE(x, t) TORCH_CHECK((x).scalar_type() == (t), #x " has the wrong dtype")
+
+void check_status(int rc, const char* what) {
+    TORCH_CHECK(rc == POPKV_OK, what, " failed (", popkv_error_string(rc), "): ", popkv_last_error());
+}
+
+int dtype_code(const at::Tensor& t) {
+    switch (t.scalar_type()) {
+        case at::kFloat: return POPKV_F32;
+        case at::kHalf: return POPKV_F16;
+        case at::kBFloat16: return POPKV_BF16;
+        default: TORCH_CHECK(false, "expected an fp32/fp16/bf16 tensor, got ", t.scalar_type());
+    }
+    return -1;
+}
+
+void* stream_of(const at::Tensor& t) {
+    return reinterpret_cast<void*>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+void check_packed(const std::vector<at::Tensor>& packed) {
+    TORCH_CHECK(packed.size() == 4, "packed cache is (k_sign, k_mag, low, delta)");
+    for (const auto& t : packed) { CHECK_CUDA(t); CHECK_CONTIGUOUS(t); }
+    CHECK_DTYPE(packed[0], at::kInt);
+    CHECK_DTYPE(packed[1], at::kInt);
+    TORCH_CHECK(packed[2].scalar_type() == at::kHalf && packed[3].scalar_type() == at::kHalf,
+                "Pop-KV representative metadata must be float16");
+    for (int i = 1; i < 4; ++i)
+        TORCH_CHECK(packed[i].sizes() == packed[0].sizes(), "packed tensors must share one shape");
+    TORCH_CHECK(packed[0].dim() == 3 || packed[0].dim() == 4,
+                "packed tensors are [KVH, capacity, words] or [B, KVH, capacity, words]");
+}
+
+std::vector<at::Tensor> pack(const at::Tensor& keys, int64_t token_capacity, int64_t flags,
+                             bool with_thresholds) {
+    CHECK_CUDA(keys); CHECK_CONTIGUOUS(keys);
+    TORCH_CHECK(keys.dim() == 3, "keys must be [KVH, T, D]");
+    TORCH_CHECK(token_capacity >= keys.size(1), "token capacity is too small");
+    c10::cuda::CUDAGuard guard(keys.device());
+    const int64_t heads = keys.size(0), tokens = keys.size(1), dim = keys.size(2);
+    const int64_t words = (dim + 31) / 32;
+    auto opts = keys.options();
+    auto k_sign = at::empty({heads, token_capacity, words}, opts.dtype(at::kInt));
+    auto k_mag = at::empty({heads, token_capacity, words}, opts.dtype(at::kInt));
+    auto low = at::empty({heads, token_capacity, words}, opts.dtype(at::kHalf));
+    auto delta = at::empty({heads, token_capacity, words}, opts.dtype(at::kHalf));
+    at::Tensor thr;
+    if (with_thresholds) thr = at::empty({heads, (tokens + 31) / 32, dim, 2}, opts.dtype(at::kFloat));
+    const int rc = popkv_pack(keys.data_ptr(), dtype_code(keys), heads, tokens, dim, tokens * dim,
+                              k_sign.data_ptr<int32_t>(), k_mag.data_ptr<int32_t>(),
+                              reinterpret_cast<uint16_t*>(low.data_ptr<at::Half>()),
+                              reinterpret_cast<uint16_t*>(delta.data_ptr<at::Half>()),
+                              token_capacity, 0, with_thresholds ? thr.data_ptr<float>() : nullptr,
+                              (int)flags, stream_of(keys));
+    check_status(rc, "popkv_pack");
+    std::vector<at::Tensor> out{k_sign, k_mag, low, delta};
+    if (with_thresholds) out.push_back(thr);
+    return out;
+}
+
+void pack_into(const at::Tensor& keys, const at::Tensor& k_sign, const at::Tensor& k_mag,
+               const at::Tensor& low, const at::Tensor& delta, int64_t token_offset,
+               int64_t flags) {
+    CHECK_CUDA(keys); CHECK_CONTIGUOUS(keys);
+    TORCH_CHECK(keys.dim() == 3, "keys must be [KVH, T, D]");
+    check_packed({k_sign, k_mag, low, delta});
+    TORCH_CHECK(k_sign.dim() == 3 && k_sign.size(0) == keys.size(0), "packed cache heads mismatch");
+    TORCH_CHECK(token_offset >= 0 && token_offset + keys.size(1) <= k_sign.size(1),
+                "Pop-KV cache capacity exceeded");
+    c10::cuda::CUDAGuard guard(keys.device());
+    const int rc = popkv_pack(keys.data_ptr(), dtype_code(keys), keys.size(0), keys.size(1),
+                              keys.size(2), keys.size(1) * keys.size(2), k_sign.data_ptr<int32_t>(),
+                              k_mag.data_ptr<int32_t>(),
+                              reinterpret_cast<uint16_t*>(low.data_ptr<at::Half>()),
+                              reinterpret_cast<uint16_t*>(delta.data_ptr<at::Half>()),
+                              k_sign.size(1), token_offset, nullptr, (int)flags, stream_of(keys));
+    check_status(rc, "popkv_pack");
+}
+
+void append(const at::Tensor& key_cache, const c10::optional<at::Tensor>& value_cache,
+            const c10::optional<at::Tensor>& new_keys, const c10::optional<at::Tensor>& new_values,
+            const at::Tensor& k_sign, const at::Tensor& k_mag, const at::Tensor& low,
+            const at::Tensor& delta, int64_t position, const c10::optional<at::Tensor>& seq_len,
+            int64_t kv_heads_per_seq, int64_t flags) {
+    CHECK_CUDA(key_cache); CHECK_CONTIGUOUS(key_cache);
+    check_packed({k_sign, k_mag, low, delta});
+    TORCH_CHECK(key_cache.dim() >= 3, "key cache is [..., heads, capacity, D]");
+    const int64_t dim = key_cache.size(-1), kv_cap = key_cache.size(-2);
+    const int64_t heads = key_cache.numel() / (kv_cap * dim);
+    const int64_t cap = k_sign.size(-2);
+    TORCH_CHECK(k_sign.numel() / (cap * k_sign.size(-1)) == heads, "packed cache heads mismatch");
+    const void* nk = nullptr;
+    const void* nv = nullptr;
+    void* vc = nullptr;
+    if (new_keys) {
+        CHECK_CUDA(*new_keys); CHECK_CONTIGUOUS(*new_keys);
+        TORCH_CHECK(new_keys->numel() == heads * dim && new_keys->scalar_type() == key_cache.scalar_type(),
+                    "new_keys must hold one row per cache head, in the cache dtype");
+        nk = new_keys->data_ptr();
+    }
+    if (value_cache && new_values) {
+        CHECK_CUDA(*value_cache); CHECK_CONTIGUOUS(*value_cache);
+        CHECK_CUDA(*new_values); CHECK_CONTIGUOUS(*new_values);
+        TORCH_CHECK(value_cache->sizes() == key_cache.sizes() && new_values->numel() == heads * dim,
+                    "value cache / new values shape mismatch");
+        vc = value_cache->data_ptr();
+        nv = new_values->data_ptr();
+    }
+    const int32_t* sl = nullptr;
+    if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
+    c10::cuda::CUDAGuard guard(key_cache.device());
+    const int rc = popkv_append(key_cache.data_ptr(), vc, dtype_code(key_cache), heads, kv_cap, dim,
+                                nk, nv, k_sign.data_ptr<int32_t>(), k_mag.data_ptr<int32_t>(),
+                                reinterpret_cast<uint16_t*>(low.data_ptr<at::Half>()),
+                                reinterpret_cast<uint16_t*>(delta.data_ptr<at::Half>()), cap, sl,
+                                position, kv_heads_per_seq, (int)flags, stream_of(key_cache));
+    check_status(rc, "popkv_append");
+}
+
+at::Tensor score(const at::Tensor& queries, const at::Tensor& k_sign, const at::Tensor& k_mag,
+                 const at::Tensor& low, const at::Tensor& delta, const at::Tensor& head_to_kv,
+                 int64_t tokens, int64_t flags, const c10::optional<at::Tensor>& seq_len,
+                 const c10::optional<at::Tensor>& out) {
+    CHECK_CUDA(queries); CHECK_CONTIGUOUS(queries);
+    TORCH_CHECK(queries.dim() == 3, "queries must be [B, QH, D]");
+    check_packed({k_sign, k_mag, low, delta});
+    CHECK_CUDA(head_to_kv); CHECK_CONTIGUOUS(head_to_kv);
+    TORCH_CHECK(head_to_kv.scalar_type() == at::kLong, "head mapping must be int64");
+    TORCH_CHECK(head_to_kv.numel() == queries.size(1), "head mapping needs one entry per query head");
+    const int64_t batch = queries.size(0), q_heads = queries.size(1), dim = queries.size(2);
+    const bool per_batch = k_sign.dim() == 4;
+    if (per_batch) TORCH_CHECK(k_sign.size(0) == batch, "batched packed cache must match the batch");
+    const int64_t kv_heads = per_batch ? k_sign.size(1) : k_sign.size(0);
+    const int64_t cap = k_sign.size(-2);
+    TORCH_CHECK(k_sign.size(-1) == (dim + 31) / 32, "packed words do not match head_dim");
+    TORCH_CHECK(tokens > 0 && tokens <= cap, "invalid score token count");
+    const int32_t* sl = nullptr;
+    if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
+    c10::cuda::CUDAGuard guard(queries.device());
+    at::Tensor scores;
+    if (out) {
+        scores = *out;
+        CHECK_CUDA(scores); CHECK_CONTIGUOUS(scores); CHECK_DTYPE(scores, at::kFloat);
+        TORCH_CHECK(scores.dim() == 3 && scores.size(0) == batch && scores.size(1) == q_heads &&
+                    scores.size(2) >= tokens, "scores out must be [B, QH, >= tokens]");
+    } else {
+        scores = at::empty({batch, q_heads, tokens}, queries.options().dtype(at::kFloat));
+    }
+    const int rc = popkv_score(queries.data_ptr(), dtype_code(queries), batch, q_heads, dim,
+                               k_sign.data_ptr<int32_t>(), k_mag.data_ptr<int32_t>(),
+                               reinterpret_cast<const uint16_t*>(low.data_ptr<at::Half>()),
+                               reinterpret_cast<const uint16_t*>(delta.data_ptr<at::Half>()),
+                               kv_heads, cap, per_batch ? 1 : 0, head_to_kv.data_ptr<int64_t>(),
+                               tokens, sl, scores.data_ptr<float>(), scores.size(2), (int)flags,
+                               stream_of(queries));
+    check_status(rc, "popkv_score");
+    return scores;
+}
+
+at::Tensor select_topk(const at::Tensor& scores, int64_t budget, int64_t tokens,
+                  const c10::optional<at::Tensor>& seq_len, int64_t rows_per_seq,
+                  const c10::optional<at::Tensor>& out) {
+    CHECK_CUDA(scores); CHECK_DTYPE(scores, at::kFloat);
+    TORCH_CHECK(scores.stride(-1) == 1, "scores rows must be contiguous");
+    const int64_t stride = scores.dim() > 1 ? scores.stride(-2) : scores.size(-1);
+    const int64_t rows = scores.numel() / std::max<int64_t>(scores.size(-1), 1);
+    TORCH_CHECK(scores.dim() == 1 || scores.is_contiguous() || scores.dim() == 2,
+                "scores must be contiguous or a 2-D row view");
+    TORCH_CHECK(tokens <= scores.size(-1), "tokens exceed the score row length");
+    const int32_t* sl = nullptr;
+    if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
+    c10::cuda::CUDAGuard guard(scores.device());
+    at::Tensor idx;
+    if (out) {
+        idx = *out;
+        CHECK_CUDA(idx); CHECK_CONTIGUOUS(idx); CHECK_DTYPE(idx, at::kInt);
+        TORCH_CHECK(idx.numel() == rows * budget, "indices out must hold rows x budget entries");
+    } else {
+        idx = at::empty({rows, budget}, scores.options().dtype(at::kInt));
+    }
+    const int rc = popkv_select(scores.data_ptr<float>(), rows, stride, tokens, sl, rows_per_seq,
+                                budget, idx.data_ptr<int32_t>(), stream_of(scores));
+    check_status(rc, "popkv_select");
+    return idx;
+}
+
+std::mutex g_ws_mutex;
+std::unordered_map<int, at::Tensor> g_workspaces;
+
+at::Tensor default_workspace(const at::Device& dev, size_t bytes) {
+    std::lock_guard<std::mutex> lock(g_ws_mutex);
+    auto& ws = g_workspaces[dev.index()];
+    if (!ws.defined() || (size_t)ws.numel() < bytes)
+        ws = at::zeros({(int64_t)bytes}, at::TensorOptions().device(dev).dtype(at::kByte));
+    return ws;
+}
+
+int64_t workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                        int64_t tokens, int64_t splits) {
+    return (int64_t)popkv_sparse_attention_workspace_bytes(batch, q_heads, kv_heads, head_dim,
+                                                           tokens, splits);
+}
+
+at::Tensor sparse_attention(const at::Tensor& queries, const at::Tensor& key_cache,
+                            const at::Tensor& value_cache,
+                            const c10::optional<at::Tensor>& indices, int64_t budget,
+                            int64_t tokens, const c10::optional<at::Tensor>& current_keys,
+                            const c10::optional<at::Tensor>& current_values,
+                            const c10::optional<at::Tensor>& seq_len,
+                            const c10::optional<at::Tensor>& workspace, int64_t splits,
+                            const c10::optional<at::Tensor>& out) {
+    CHECK_CUDA(queries); CHECK_CONTIGUOUS(queries);
+    CHECK_CUDA(key_cache); CHECK_CONTIGUOUS(key_cache);
+    CHECK_CUDA(value_cache); CHECK_CONTIGUOUS(value_cache);
+    TORCH_CHECK(queries.dim() == 3, "queries must be [B, QH, D]");
+    TORCH_CHECK(key_cache.sizes() == value_cache.sizes(), "key and value caches differ in shape");
+    TORCH_CHECK(key_cache.scalar_type() == queries.scalar_type() &&
+                value_cache.scalar_type() == queries.scalar_type(),
+                "queries and caches must share one dtype");
+    const int64_t batch = queries.size(0), q_heads = queries.size(1), dim = queries.size(2);
+    TORCH_CHECK(key_cache.dim() == 3 || key_cache.dim() == 4,
+                "caches are [KVH, capacity, D] (shared) or [B, KVH, capacity, D]");
+    TORCH_CHECK(key_cache.size(-1) == dim, "cache head_dim mismatch");
+    const bool per_batch = key_cache.dim() == 4;
+    const int64_t kv_heads = key_cache.dim() == 4 ? key_cache.size(1) : key_cache.size(0);
+    if (key_cache.dim() == 4) TORCH_CHECK(key_cache.size(0) == batch, "batched caches must match the batch");
+    const int64_t kv_cap = key_cache.size(-2);
+    const void* ck = nullptr;
+    const void* cv = nullptr;
+    if (current_keys || current_values) {
+        TORCH_CHECK(current_keys && current_values, "current_keys and current_values go together");
+        CHECK_CUDA(*current_keys); CHECK_CONTIGUOUS(*current_keys);
+        CHECK_CUDA(*current_values); CHECK_CONTIGUOUS(*current_values);
+        TORCH_CHECK(current_keys->numel() == batch * kv_heads * dim &&
+                    current_values->numel() == batch * kv_heads * dim,
+                    "current rows must be [B, KVH, D]");
+        TORCH_CHECK(current_keys->scalar_type() == queries.scalar_type() &&
+                    current_values->scalar_type() == queries.scalar_type(), "current rows dtype");
+        ck = current_keys->data_ptr();
+        cv = current_values->data_ptr();
+    }
+    const int32_t* idx = nullptr;
+    int64_t idx_stride = 0;
+    if (indices) {
+        CHECK_CUDA(*indices); CHECK_CONTIGUOUS(*indices); CHECK_DTYPE(*indices, at::kInt);
+        TORCH_CHECK(indices->numel() % (batch * q_heads) == 0, "indices must be [B*QH, n]");
+        idx_stride = indices->numel() / (batch * q_heads);
+        TORCH_CHECK(idx_stride >= budget, "indices rows shorter than budget");
+        idx = indices->data_ptr<int32_t>();
+    }
+    const int32_t* sl = nullptr;
+    if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
+    c10::cuda::CUDAGuard guard(queries.device());
+    const size_t need = popkv_sparse_attention_workspace_bytes(batch, q_heads, kv_heads, dim, tokens, splits);
+    at::Tensor ws;
+    if (workspace) {
+        ws = *workspace;
+        CHECK_CUDA(ws); CHECK_CONTIGUOUS(ws);
+        TORCH_CHECK((size_t)ws.nbytes() >= need, "workspace too small: ", ws.nbytes(), " < ", need);
+    } else {
+        ws = default_workspace(queries.device(), need);
+    }
+    at::Tensor o = out ? *out : at::empty_like(queries);
+    if (out) {
+        CHECK_CUDA(o); CHECK_CONTIGUOUS(o);
+        TORCH_CHECK(o.sizes() == queries.sizes() && o.scalar_type() == queries.scalar_type(), "out shape/dtype");
+    }
+    const int rc = popkv_sparse_attention(
+        queries.data_ptr(), dtype_code(queries), batch, q_heads, dim, key_cache.data_ptr(),
+        value_cache.data_ptr(), kv_heads, kv_cap, per_batch ? 1 : 0, ck, cv, idx, idx_stride,
+        budget, tokens, sl, o.data_ptr(), ws.data_ptr(), (size_t)ws.nbytes(), splits,
+        stream_of(queries));
+    check_status(rc, "popkv_sparse_attention");
+    return o;
+}
+
+void advance(const at::Tensor& seq_len, int64_t increment) {
+    CHECK_CUDA(seq_len); CHECK_CONTIGUOUS(seq_len); CHECK_DTYPE(seq_len, at::kInt);
+    c10::cuda::CUDAGuard guard(seq_len.device());
+    check_status(popkv_advance(seq_len.data_ptr<int32_t>(), seq_len.numel(), (int32_t)increment,
+                               stream_of(seq_len)),
+                 "popkv_advance");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.doc() = "Pop-KV retrieval on B200 (sm_100a): torch front end of the C ABI";
+    m.def("pack", &pack, py::arg("keys"), py::arg("token_capacity"), py::arg("flags") = 0,
+          py::arg("with_thresholds") = false);
+    m.def("pack_into", &pack_into, py::arg("keys"), py::arg("k_sign"), py::arg("k_mag"),
+          py::arg("low"), py::arg("delta"), py::arg("token_offset"), py::arg("flags") = 0);
+    m.def("append", &append, py::arg("key_cache"), py::arg("value_cache"), py::arg("new_keys"),
+          py::arg("new_values"), py::arg("k_sign"), py::arg("k_mag"), py::arg("low"),
+          py::arg("delta"), py::arg("position"), py::arg("seq_len") = py::none(),
+          py::arg("kv_heads_per_seq") = 0, py::arg("flags") = 0);
+    m.def("score", &score, py::arg("queries"), py::arg("k_sign"), py::arg("k_mag"), py::arg("low"),
+          py::arg("delta"), py::arg("head_to_kv"), py::arg("tokens"), py::arg("flags") = 0,
+          py::arg("seq_len") = py::none(), py::arg("out") = py::none());
+    m.def("select", &select_topk, py::arg("scores"), py::arg("budget"), py::arg("tokens"),
+          py::arg("seq_len") = py::none(), py::arg("rows_per_seq") = 0, py::arg("out") = py::none());
+    m.def("sparse_attention", &sparse_attention, py::arg("queries"), py::arg("key_cache"),
+          py::arg("value_cache"), py::arg("indices"), py::arg("budget"), py::arg("tokens"),
+          py::arg("current_keys") = py::none(), py::arg("current_values") = py::none(),
+          py::arg("seq_len") = py::none(), py::arg("workspace") = py::none(),
+          py::arg("splits") = 0, py::arg("out") = py::none());
+    m.def("workspace_bytes", &workspace_bytes);
+    m.def("advance", &advance);
+    m.def("version", &popkv_version);
+}

@@ -1,0 +1,157 @@
+"""Pop-KV CUDA entry points on B200 (sm_100a).
+
+Drop-in for the reference module ``popkv_cuda.py`` (kw78999/FIER-2bits): the same
+``pack_keys`` / ``pack_keys_into`` / ``score`` signatures, argument meaning and
+errors (``ValueError`` for non-3-D, non-CUDA or non-contiguous inputs,
+popkv_cuda.py:27-28,34-35,41-42; ``RuntimeError`` without a GPU, popkv_cuda.py:14-15;
+``RuntimeError`` from the native checks, csrc/popkv_ext.cu:199-241), plus the rest
+of the decode-time retrieval path as native kernels:
+
+  append_keys        static-cache write + open-group re-pack   (popkv.py:270-280, 487-495)
+  select             top-(budget-1) + newest token              (popkv.py:594-600, 141-145)
+  sparse_attention   fused gather + exact split-K attention     (popkv.py:341-368)
+  retrieve           score -> select -> sparse_attention
+
+Every call is asynchronous on the current CUDA stream and goes through the thin
+torch extension ``lib/_popkv_torch*.so`` over the C ABI ``libpopkv_b200.so``.
+There is no CPU fallback: without the built extension or a GPU, calls raise.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from _native import extension
+
+# Flag: divide like a --use_fast_math build of the reference extension (see the C header).
+REFERENCE_DIVISION = 1
+
+
+def _packed(packed) -> Sequence[torch.Tensor]:
+    if len(packed) != 4:
+        raise ValueError("packed cache is (k_sign, k_mag, low, delta)")
+    return packed
+
+
+def pack_keys(keys: torch.Tensor, *, token_capacity: int | None = None, flags: int = 0,
+              with_thresholds: bool = False):
+    """Pack K sign/magnitude plus FP16 low/delta representatives (group size 32).
+
+    keys [KV heads, tokens, head dim] (fp32/fp16/bf16) -> (k_sign int32, k_mag int32,
+    low fp16, delta fp16), each [KV heads, token_capacity, ceil(D/32)].  With
+    ``with_thresholds`` a fifth tensor [KVH, groups, D, 2] holds (min/2, max/2).
+    """
+    if keys.ndim != 3 or not keys.is_cuda or not keys.is_contiguous():
+        raise ValueError("keys must be contiguous CUDA [KV heads, tokens, head dim]")
+    capacity = int(keys.shape[1]) if token_capacity is None else int(token_capacity)
+    return tuple(extension().pack(keys, capacity, int(flags), bool(with_thresholds)))
+
+
+def pack_keys_into(keys: torch.Tensor, packed, *, token_offset: int, flags: int = 0) -> None:
+    """Pack ``keys`` into rows token_offset.. of caller-owned packed tensors."""
+    if keys.ndim != 3 or not keys.is_cuda or not keys.is_contiguous():
+        raise ValueError("keys must be contiguous CUDA [KV heads, tokens, head dim]")
+    extension().pack_into(keys, *_packed(packed), int(token_offset), int(flags))
+
+
+def score(queries: torch.Tensor, packed, *, head_to_kv: torch.Tensor, tokens: int,
+          flags: int = 0, seq_len: torch.Tensor | None = None,
+          out: torch.Tensor | None = None) -> torch.Tensor:
+    """Return Pop-KV approximate QK scores for every query head and token.
+
+    queries [B, QH, D]; packed [KVH, cap, W] (shared by the batch, as in the
+    reference) or [B, KVH, cap, W] (one cache per sequence) -> fp32 [B, QH, tokens].
+    """
+    if queries.ndim != 3 or not queries.is_cuda or not queries.is_contiguous():
+        raise ValueError("queries must be contiguous CUDA [batch, query heads, head dim]")
+    return extension().score(queries, *_packed(packed), head_to_kv.contiguous(), int(tokens),
+                             int(flags), seq_len, out)
+
+
+def append_keys(key_cache: torch.Tensor, value_cache: torch.Tensor | None, new_keys,
+                new_values, packed, *, position: int, seq_len: torch.Tensor | None = None,
+                kv_heads_per_seq: int = 0, flags: int = 0) -> None:
+    """Write the new token's k/v at ``position`` and re-pack its open 32-token group.
+
+    key_cache/value_cache [..., heads, kv_capacity, D]; new_keys/new_values one row
+    per cache head.  With ``seq_len`` (int32 device [B]) the position of sequence b
+    is seq_len[b] and ``position`` is ignored.
+    """
+    if not key_cache.is_cuda or not key_cache.is_contiguous():
+        raise ValueError("key_cache must be a contiguous CUDA tensor")
+    extension().append(key_cache, value_cache, new_keys, new_values, *_packed(packed),
+                       int(position), seq_len, int(kv_heads_per_seq), int(flags))
+
+
+def select(scores: torch.Tensor, *, budget: int, tokens: int | None = None,
+           seq_len: torch.Tensor | None = None, rows_per_seq: int = 0,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Top-(budget-1) token indices per row plus the newest token.
+
+    scores [..., L] fp32 -> int32 [rows, budget]: the min(budget-1, L) best tokens in
+    ascending index order (ties to the lowest index), then L, then -1 padding.
+    """
+    if not scores.is_cuda or scores.dtype != torch.float32:
+        raise ValueError("scores must be a CUDA float32 tensor")
+    if int(budget) <= 1:
+        raise ValueError("budget must reserve at least one retrieved and one current token")
+    tokens = int(scores.shape[-1]) if tokens is None else int(tokens)
+    return extension().select(scores, int(budget), tokens, seq_len, int(rows_per_seq), out)
+
+
+def sparse_attention(queries: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                     indices: torch.Tensor | None, *, budget: int, tokens: int,
+                     current_keys: torch.Tensor | None = None,
+                     current_values: torch.Tensor | None = None,
+                     seq_len: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                     splits: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Exact attention of every query head over its selected tokens.
+
+    queries [B, QH, D]; caches [KVH, kv_cap, D] (shared) or [B, KVH, kv_cap, D];
+    indices int32 [B*QH, >= budget] (e.g. from ``select``; int64 is converted) or
+    None for dense attention over tokens 0..L.  Token L is read from
+    current_keys/current_values [B, KVH, D] when given.  Returns [B, QH, D].
+    """
+    if queries.ndim != 3 or not queries.is_cuda or not queries.is_contiguous():
+        raise ValueError("queries must be contiguous CUDA [batch, query heads, head dim]")
+    if indices is not None and indices.dtype != torch.int32:
+        indices = indices.to(torch.int32)
+    if indices is not None:
+        indices = indices.contiguous()
+    return extension().sparse_attention(queries, key_cache, value_cache, indices, int(budget),
+                                        int(tokens), current_keys, current_values, seq_len,
+                                        workspace, int(splits), out)
+
+
+def workspace_bytes(batch: int, q_heads: int, kv_heads: int, head_dim: int, tokens: int,
+                    splits: int = 0) -> int:
+    return int(extension().workspace_bytes(batch, q_heads, kv_heads, head_dim, tokens, splits))
+
+
+def new_workspace(batch: int, q_heads: int, kv_heads: int, head_dim: int, tokens: int,
+                  device, splits: int = 0) -> torch.Tensor:
+    """Zero-filled attention workspace (the kernels keep it reusable)."""
+    n = workspace_bytes(batch, q_heads, kv_heads, head_dim, tokens, splits)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def advance(seq_len: torch.Tensor, increment: int = 1) -> None:
+    extension().advance(seq_len, int(increment))
+
+
+def retrieve(queries: torch.Tensor, packed, key_cache: torch.Tensor, value_cache: torch.Tensor,
+             *, head_to_kv: torch.Tensor, tokens: int, budget: int,
+             current_keys: torch.Tensor | None = None, current_values: torch.Tensor | None = None,
+             seq_len: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+             flags: int = 0):
+    """score -> select -> sparse_attention for one layer; returns (out, indices)."""
+    scores = score(queries, packed, head_to_kv=head_to_kv, tokens=tokens, flags=flags,
+                   seq_len=seq_len)
+    rows_per_seq = int(queries.shape[1])
+    indices = select(scores.view(-1, scores.shape[-1]), budget=budget, tokens=tokens,
+                     seq_len=seq_len, rows_per_seq=rows_per_seq)
+    out = sparse_attention(queries, key_cache, value_cache, indices, budget=budget,
+                           tokens=tokens, current_keys=current_keys,
+                           current_values=current_values, seq_len=seq_len, workspace=workspace)
+    return out, indices

@@ -1,0 +1,164 @@
+/*
+ * popkv_b200.h -- C ABI of the B200 (sm_100a) Pop-KV retrieval library.
+ *
+ * Plain pointers and sizes only: every pointer argument is a device pointer
+ * unless stated otherwise, every call is asynchronous on `stream`
+ * (a cudaStream_t, passed as void*; NULL = legacy default stream), and every
+ * call returns POPKV_OK or an error code (see popkv_error_string /
+ * popkv_last_error).  Argument checks happen on the host before anything is
+ * launched, so an error return means nothing was enqueued.
+ *
+ * Packed key cache (identical to the reference layout, csrc/popkv_ext.cu:204-208):
+ *   k_sign, k_mag : int32  [cache_heads, capacity, words]   bit i of word w = channel 32w+i
+ *   low, delta    : fp16   [cache_heads, capacity, words]   (passed as uint16 bit patterns)
+ *   words = ceil(head_dim / 32); element (h, t, w) at (h*capacity + t)*words + w.
+ *
+ * Batched caches (an extension of the reference, whose batch rows share one cache):
+ * with cache_per_batch != 0 the cache heads are [batch, kv_heads] flattened,
+ * and sequence b owns heads b*kv_heads .. b*kv_heads+kv_heads-1.
+ *
+ * Sequence lengths: calls take a host `tokens` (the prefix length L, or an upper
+ * bound) and an optional device `seq_len` array [batch] (int32).  When seq_len is
+ * given, row b uses min(seq_len[b], tokens) -- this keeps launches identical from
+ * step to step, so a whole decode step can be captured once in a CUDA graph.
+ */
+#ifndef POPKV_B200_H
+#define POPKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* popkv_stream_t;
+
+enum popkv_status {
+    POPKV_OK = 0,
+    POPKV_ERR_INVALID_ARGUMENT = 1,
+    POPKV_ERR_CAPACITY = 2,
+    POPKV_ERR_UNSUPPORTED = 3,
+    POPKV_ERR_ALIGNMENT = 4,
+    POPKV_ERR_CUDA = 5,
+    POPKV_ERR_WORKSPACE = 6
+};
+
+enum popkv_dtype { POPKV_F32 = 0, POPKV_F16 = 1, POPKV_BF16 = 2 };
+
+/* Flags for pack / append / score. */
+enum popkv_flags {
+    /* Divide the representative sums with the PTX div.full.ftz.f32 instruction and
+     * scale scores by rsqrtf(D), as a --use_fast_math build of the reference
+     * extension does (popkv_cuda.py:20).  Default: IEEE division, 1/sqrt(D)
+     * correctly rounded on the host. */
+    POPKV_FLAG_REFERENCE_DIVISION = 1
+};
+
+/* Static description of an error code. */
+const char* popkv_error_string(int status);
+/* Detail message of the last error raised by a call on this host thread. */
+const char* popkv_last_error(void);
+/* Library version (major*10000 + minor*100 + patch). */
+int popkv_version(void);
+
+/*
+ * (a) Key packer.  Replaces popkv_pack_cuda / popkv_pack_into_cuda
+ * (csrc/popkv_ext.cu:198-227, bound as `pack` / `pack_into` in csrc/popkv_ext.cpp:13-14).
+ *
+ * keys: [heads, tokens, head_dim] rows of `dtype`, head h starting at
+ *       keys + h*key_head_stride elements (key_head_stride >= tokens*head_dim).
+ * Tokens are grouped in 32s from the first input row; input row t is written to
+ * packed row token_offset + t of every head.  Requires token_offset + tokens <= capacity.
+ * thresholds (nullable): fp32 [heads, ceil(tokens/32), head_dim, 2] = (min*0.5, max*0.5).
+ */
+int popkv_pack(const void* keys, int dtype, int64_t heads, int64_t tokens, int64_t head_dim,
+               int64_t key_head_stride, int32_t* k_sign, int32_t* k_mag, uint16_t* low,
+               uint16_t* delta, int64_t capacity, int64_t token_offset, float* thresholds,
+               int flags, popkv_stream_t stream);
+
+/*
+ * (b) Incremental append with open-group re-pack.  Replaces append_popkv + the static
+ * cache write (popkv.py:270-280, popkv.py:487-495): one launch per layer, no host copies.
+ *
+ * For every cache head h (sequence b = h / kv_heads_per_seq) with position
+ * P = seq_len ? seq_len[b] : position:
+ *   key_cache[h, P] = new_keys[h], value_cache[h, P] = new_values[h]   (when non-NULL),
+ *   then re-packs the open group rows floor(P/32)*32 .. P of the packed cache from
+ *   key_cache (row P taken from new_keys), exactly as pack_keys_into of the open group.
+ * key_cache/value_cache: [heads, kv_capacity, head_dim]; new_keys/new_values: [heads, head_dim].
+ * new_keys may be NULL when row P of key_cache already holds the new key
+ * (then value arguments are ignored).  Heads whose P >= min(capacity, kv_capacity) are
+ * skipped on the device (callers check capacity on the host).
+ */
+int popkv_append(void* key_cache, void* value_cache, int dtype, int64_t heads,
+                 int64_t kv_capacity, int64_t head_dim, const void* new_keys,
+                 const void* new_values, int32_t* k_sign, int32_t* k_mag, uint16_t* low,
+                 uint16_t* delta, int64_t capacity, const int32_t* seq_len, int64_t position,
+                 int64_t kv_heads_per_seq, int flags, popkv_stream_t stream);
+
+/*
+ * (c)+(d) Query packer fused with the popcount scorer.  Replaces popkv_score_cuda
+ * (csrc/popkv_ext.cu:229-254, bound as `score` in csrc/popkv_ext.cpp:15).
+ *
+ * queries: [batch, q_heads, head_dim] of q_dtype; head_to_kv: int64 [q_heads] (device).
+ * scores: fp32 [batch, q_heads, score_stride]; tokens 0..L-1 of every row are written.
+ * Requires tokens <= capacity and tokens <= score_stride.
+ */
+int popkv_score(const void* queries, int q_dtype, int64_t batch, int64_t q_heads,
+                int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                const uint16_t* low, const uint16_t* delta, int64_t kv_heads, int64_t capacity,
+                int cache_per_batch, const int64_t* head_to_kv, int64_t tokens,
+                const int32_t* seq_len, float* scores, int64_t score_stride, int flags,
+                popkv_stream_t stream);
+
+/*
+ * (e) Per-row top-(budget-1) with the newest token reserved.  Replaces
+ * torch.topk(sorted=False) + _append_current (popkv.py:594-600, 141-145).
+ *
+ * scores: fp32 [rows, score_stride]; row r (sequence r / rows_per_seq) has L tokens.
+ * indices: int32 [rows, budget]: the k = min(budget-1, L) largest scores' token
+ * indices in ascending index order (ties -> lowest index; -0.0 == +0.0), then L,
+ * then -1 padding.
+ */
+int popkv_select(const float* scores, int64_t rows, int64_t score_stride, int64_t tokens,
+                 const int32_t* seq_len, int64_t rows_per_seq, int64_t budget,
+                 int32_t* indices, popkv_stream_t stream);
+
+/*
+ * (f) Fused gather + exact split-K decode attention.  Replaces gather_selected_kv +
+ * selected_attention (popkv.py:341-368) without materialising the gathered rows.
+ *
+ * queries/out: [batch, q_heads, head_dim]; key_cache/value_cache: [cache_heads,
+ * kv_capacity, head_dim]; all of `dtype`.  Query head qh reads KV head qh / G with
+ * G = q_heads / kv_heads (the decoder's head_to_kv = arange(QH) // G, popkv.py:427);
+ * G must be <= 16.  current_keys/current_values ([batch, kv_heads, head_dim],
+ * nullable): the rows used for token index L (the newest token, not yet in the
+ * cache); when NULL row L is read from the caches.
+ * indices: int32 [batch*q_heads, index_stride]; the first min(budget-1, L)+1 entries
+ * of each row are the attended tokens (any order, entries outside 0..L ignored), e.g.
+ * the output of popkv_select.  indices == NULL selects dense attention over 0..L.
+ * Scale 1/sqrt(head_dim), softmax and accumulation in fp32.
+ * workspace: device buffer of popkv_sparse_attention_workspace_bytes(); it must be
+ * zero-filled once after allocation (every call leaves it zeroed where it must be).
+ * Calls that share a workspace must not overlap on the GPU.
+ * splits: number of token segments per (sequence, KV head); 0 = automatic.
+ */
+size_t popkv_sparse_attention_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                              int64_t head_dim, int64_t tokens, int64_t splits);
+int popkv_sparse_attention(const void* queries, int dtype, int64_t batch, int64_t q_heads,
+                           int64_t head_dim, const void* key_cache, const void* value_cache,
+                           int64_t kv_heads, int64_t kv_capacity, int cache_per_batch,
+                           const void* current_keys, const void* current_values,
+                           const int32_t* indices, int64_t index_stride, int64_t budget,
+                           int64_t tokens, const int32_t* seq_len, void* out, void* workspace,
+                           size_t workspace_bytes, int64_t splits, popkv_stream_t stream);
+
+/* Adds `increment` to seq_len[0..batch-1] on the device (end of a decode step). */
+int popkv_advance(int32_t* seq_len, int64_t batch, int32_t increment, popkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POPKV_B200_H */

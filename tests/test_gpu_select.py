@@ -1,0 +1,79 @@
+"""(e) top-(budget-1) selection with the newest token reserved: bit-exact index sets
+(ties to the lowest index) against the oracle; the reference's torch.topk agrees
+as a set wherever the threshold is tie-free."""
+import numpy as np
+import pytest
+import torch
+
+import popkv_cuda as pk
+import popkv_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _check(scores: torch.Tensor, budget: int, lengths=None, rows_per_seq=0):
+    tokens = scores.shape[-1]
+    sl = None if lengths is None else torch.tensor(lengths, dtype=torch.int32, device=DEV)
+    got = pk.select(scores.to(DEV), budget=budget, tokens=tokens, seq_len=sl,
+                    rows_per_seq=rows_per_seq).cpu().numpy()
+    rows = scores.shape[0]
+    per_row = None if lengths is None else np.repeat(lengths, rows_per_seq)[:rows]
+    ref = O.select(scores.numpy(), budget=budget, lengths=per_row)
+    np.testing.assert_array_equal(got, ref)
+    return got
+
+
+@pytest.mark.parametrize("L,budget", [(1, 2), (5, 2), (100, 17), (64, 65), (50, 51), (50, 4096),
+                                      (1000, 128), (4096, 1024), (32768, 4096), (40000, 4096),
+                                      (131072, 4096), (300000, 8192)])
+def test_select_random(L, budget):
+    g = torch.Generator().manual_seed(L + budget)
+    scores = torch.randn(6, L, generator=g) * 5
+    _check(scores, budget)
+
+
+def test_select_matches_reference_topk_sets(golden):
+    for case in ("select_L100_b17", "select_L64_b65", "select_L50_b51", "select_L300_b128"):
+        scores = torch.from_numpy(golden[f"{case}/scores"][0])
+        budget = int(case.split("_b")[1])
+        got = _check(scores, budget)
+        exp = golden[f"{case}/indices_sorted"]
+        k = min(budget - 1, scores.shape[-1])
+        np.testing.assert_array_equal(got[:, : k + 1], exp)
+
+
+def test_select_ties_and_signed_zero():
+    L = 5000
+    scores = torch.zeros(4, L)
+    scores[1, ::7] = 1.0               # ties above the threshold
+    scores[2] = torch.randint(0, 3, (L,), generator=torch.Generator().manual_seed(1)).float()
+    scores[3, ::2] = -0.0              # -0.0 ties with +0.0
+    _check(scores, 300)
+
+
+def test_select_quantised_scores_many_ties():
+    g = torch.Generator().manual_seed(3)
+    scores = (torch.randn(32, 32768, generator=g) * 4).round() / 4
+    _check(scores, 4096)
+
+
+def test_select_device_lengths():
+    g = torch.Generator().manual_seed(4)
+    scores = torch.randn(3 * 8, 20000, generator=g)
+    _check(scores, 1024, lengths=[20000, 700, 1023], rows_per_seq=8)
+
+
+def test_select_agrees_with_torch_topk_as_sets():
+    g = torch.Generator().manual_seed(5)
+    scores = torch.randn(32, 32768, generator=g)
+    got = pk.select(scores.to(DEV), budget=4096).cpu()
+    ref = torch.topk(scores.to(DEV), k=4095, dim=-1, sorted=False).indices.cpu()
+    for r in range(32):
+        assert set(got[r, :4095].tolist()) == set(ref[r].tolist())
+        assert got[r, 4095] == 32768
+
+
+def test_select_rejects_budget_one():
+    with pytest.raises(ValueError):
+        pk.select(torch.zeros(2, 10, device=DEV), budget=1)
