@@ -43,8 +43,8 @@ PACKED_BYTES = 48  # per token per KV head at D = 128
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--context", type=int, default=32768)
@@ -63,24 +63,27 @@ def measured_peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi sampling (every 100 ms) filtered to the timed window afterwards."""
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index: int):
         self.index, self.proc, self.lines = index, None, []
+        self.window = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
         return self
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -91,24 +94,27 @@ class ClockSampler:
             self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        import datetime as dt
+        rows = []
         for line in self.lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                ts = dt.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[1]), float(f[2]), [n for n, v in zip(self.NAMES, f[5:9])
+                                                            if v.lower() == "active"]))
             except ValueError:
                 continue
-            for name, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        t0, t1 = self.window or (rows[0][0], rows[-1][0])
+        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05]
+        picked = inside or [min(rows, key=lambda r: abs(r[0] - (t0 + t1) / 2))]
+        reasons = sorted({n for r in picked for n in r[3]})
+        return {"sm_mhz": statistics.median(r[1] for r in picked), "sm_max_mhz": picked[-1][2],
+                "reasons": reasons, "samples_in_window": len(inside),
+                "window_s": round(t1 - t0, 3)}
 
 
 # --------------------------------------------------------------- CPU paths
@@ -165,9 +171,10 @@ def run_ours(args):
         group = dist.group.WORLD
     layers, L0, budget = args.layers, args.context, args.budget
     B = world  # weak scaling: one sequence per GPU, sharded by KV head
-    total_steps = args.warmup + args.steps + 2
+    total_steps = min(args.warmup + args.steps + 2, 64)  # distinct per-step inputs, reused cyclically
+    reserve = args.warmup + 2 * args.steps + 4
     stack = popkv.RetrievalStack(layers=layers, batch=B, kv_heads=KVH, q_heads=QH, head_dim=D,
-                                 max_tokens=L0 + total_steps + 1, budget=budget,
+                                 max_tokens=L0 + reserve, budget=budget,
                                  dtype=torch.bfloat16, device=dev, process_group=group)
     (k0, k1), (q0, q1) = stack.kv_range, stack.q_range
     gens = []
@@ -191,12 +198,14 @@ def run_ours(args):
         qs.append(torch.stack(q_l)); ks.append(torch.stack(k_l)); vs.append(torch.stack(v_l))
     torch.cuda.synchronize()
 
+    clocks = ClockSampler(local).start()
     # Warm-up (eager first step, then graph capture, then graph replays).
     stack.step(qs[0], ks[0], vs[0])
     stack.capture()
     step_idx = 1
     for _ in range(max(args.warmup - 1, 0)):
-        stack.step(qs[step_idx], ks[step_idx], vs[step_idx]); step_idx += 1
+        j = step_idx % total_steps
+        stack.step(qs[j], ks[j], vs[j]); step_idx += 1
     torch.cuda.synchronize()
 
     def barrier():
@@ -207,12 +216,16 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(); torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            stack.step(qs[step_idx], ks[step_idx], vs[step_idx]); step_idx += 1
-        end.record(stream)
-        torch.cuda.synchronize()
+    w0 = time.time()
+    start.record(stream)
+    for s in range(args.steps):
+        j = step_idx + s
+        stack.step(qs[j % total_steps], ks[j % total_steps], vs[j % total_steps])
+    end.record(stream)
+    torch.cuda.synchronize()
+    clocks.window = (w0, time.time())
+    time.sleep(0.3)
+    clocks.stop()
     barrier()
     elapsed = torch.tensor([start.elapsed_time(end)], device=dev)
     if world > 1:
@@ -222,7 +235,7 @@ def run_ours(args):
 
     # ---- per-stage timing (idempotent re-runs of each stage over all layers, no advance).
     stage_ms = {}
-    reps = 3
+    reps = 20
     tokens = stack.max_tokens
 
     def run_stage(name, i):
@@ -242,21 +255,31 @@ def run_ours(args):
                            stack.packed[i], position=0, seq_len=stack.seq_len,
                            kv_heads_per_seq=stack.kv_heads)
 
+    def stage_graph(name):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                for i in range(layers):
+                    run_stage(name, i)
+        stream.wait_stream(side)
+        return g
+
     for name in ("score", "select", "attention", "append"):
         for i in range(layers):
-            run_stage(name, i)  # warm
+            run_stage(name, i)  # eager warm-up of this stage
+        g = stage_graph(name)
+        g.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         for _ in range(reps):
-            for i in range(layers):
-                if name == "select":
-                    run_stage("score", i)  # select needs this layer's scores
-                run_stage(name, i)
+            g.replay()
         b.record(stream)
         torch.cuda.synchronize()
         stage_ms[name] = a.elapsed_time(b) / (reps * layers)
-    stage_ms["select"] -= stage_ms["score"]
+        del g
 
     # Union of selections per (sequence, KV head) -> attention's algorithmic bytes.
     L_now = stack.length
@@ -279,9 +302,9 @@ def run_ours(args):
     step_bytes = sum(nbytes[n] for n in ("score", "select", "attention", "append"))
 
     # ---- e2e: public API with pinned host inputs and outputs, copies inside the region.
-    host_q = [qs[s % total_steps].cpu().pin_memory() for s in range(args.steps)]
-    host_k = [ks[s % total_steps].cpu().pin_memory() for s in range(args.steps)]
-    host_v = [vs[s % total_steps].cpu().pin_memory() for s in range(args.steps)]
+    host_q = [qs[s].cpu().pin_memory() for s in range(total_steps)]
+    host_k = [ks[s].cpu().pin_memory() for s in range(total_steps)]
+    host_v = [vs[s].cpu().pin_memory() for s in range(total_steps)]
     out_shape = (stack.gathered if world > 1 else stack.out).shape
     host_out = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
     # Reset lengths so the e2e steps stay inside the reserve.
@@ -289,8 +312,9 @@ def run_ours(args):
     torch.cuda.synchronize(); barrier()
     t0 = time.perf_counter()
     for s in range(args.steps):
-        res = stack.step(host_q[s].to(dev, non_blocking=True), host_k[s].to(dev, non_blocking=True),
-                         host_v[s].to(dev, non_blocking=True))
+        j = s % total_steps
+        res = stack.step(host_q[j].to(dev, non_blocking=True), host_k[j].to(dev, non_blocking=True),
+                         host_v[j].to(dev, non_blocking=True))
         host_out.copy_(res, non_blocking=True)
     torch.cuda.synchronize()
     e2e_ms = torch.tensor([(time.perf_counter() - t0) * 1e3], device=dev)

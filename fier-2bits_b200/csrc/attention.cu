@@ -195,17 +195,28 @@ __device__ void finish_and_combine(const AttnParams& p, int b, int kvh, float* s
         s_l[h * S] = 1.0f / lsum;  // s_l row h, slot 0 now holds 1/L
     }
     __syncthreads();
+    // Every (head, channel) output sums S partials: issue the loads 8 at a time so
+    // the L2 latency overlaps (empty segments carry weight 0 and zero partials).
     T* out = static_cast<T*>(p.out);
     for (int i = threadIdx.x; i < p.G * p.D; i += blockDim.x) {
         const int h = i / p.D;
         const int d = i - h * p.D;
         const float* acc = p.ws_acc + (row0 + h) * S * p.D + d;
-        float o = 0.0f;
-        for (int s = 0; s < S; ++s) {
-            const float w = s_w[h * S + s];
-            if (w != 0.0f) o += w * __ldcg(acc + static_cast<int64_t>(s) * p.D);
+        const float* w = s_w + h * S;
+        float o0 = 0.0f, o1 = 0.0f;
+        int s = 0;
+        for (; s + 8 <= S; s += 8) {
+            float a[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = __ldcg(acc + static_cast<int64_t>(s + j) * p.D);
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                o0 = fmaf(w[s + j], a[j], o0);
+                o1 = fmaf(w[s + j + 1], a[j + 1], o1);
+            }
         }
-        out[(row0 + h) * p.D + d] = from_float<T>(o * s_l[h * S]);
+        for (; s < S; ++s) o0 = fmaf(w[s], __ldcg(acc + static_cast<int64_t>(s) * p.D), o0);
+        out[(row0 + h) * p.D + d] = from_float<T>((o0 + o1) * s_l[h * S]);
     }
     if (threadIdx.x == 0) p.tickets[b * p.KVH + kvh] = 0u;
 }

@@ -5,15 +5,16 @@
 // scores' token indices in ascending index order, ties at the threshold broken
 // towards the lowest index, then L (the newest token), then -1 padding.
 //
-// B200 design: one thread-block cluster of C CTAs per row (C <= 8).  Each CTA
-// stages its slice of the row in shared memory as order-preserving uint32 keys
+// B200 design: one thread-block cluster of C CTAs per row (C <= 8, the smallest
+// that lets each CTA hold its slice: rows up to 32K tokens run as one CTA with the
+// whole row in shared memory).  Each CTA stages its slice as order-preserving uint32 keys
 // and the cluster runs an exact 3-pass radix select (11/11/10-bit digits): each
 // CTA builds a histogram of its candidates (warp-aggregated with match.any), the
 // cluster reads all histograms through distributed shared memory, and every CTA
 // derives the same threshold digit.  A final pass ranks the keys above the
 // threshold and the lowest-indexed ties with warp ballots and a cluster-wide
 // prefix over CTA counts, so the selection is written in index order without a
-// sort.  Rows longer than C x 16384 keys are re-read from global memory (L2) in
+// sort.  Rows longer than 8 x 32768 keys are re-read from global memory (L2) in
 // every pass instead of being staged.  Cluster barriers are hardware barriers;
 // no CTA spins on memory.
 #include <cooperative_groups.h>
@@ -25,10 +26,10 @@ namespace cg = cooperative_groups;
 namespace popkv {
 namespace {
 
-constexpr int kSelThreads = 512;
+constexpr int kSelThreads = 1024;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kBins = 2048;
-constexpr int kResidentMax = 16384;  // keys staged per CTA (64 KB)
+constexpr int kResidentMax = 32768;  // keys staged per CTA (128 KB)
 
 struct SelectShared {
     uint32_t hist[2][kBins];
@@ -40,14 +41,13 @@ struct SelectShared {
     uint32_t sel_bin, sel_above;
 };
 
-template <bool RESIDENT>
+template <bool RESIDENT, int C>
 __global__ void __launch_bounds__(kSelThreads)
 select_kernel(const float* __restrict__ scores, int64_t stride, int64_t tokens,
               const int32_t* __restrict__ seq_len, int64_t rows_per_seq, int64_t budget,
               int32_t* __restrict__ indices, bool vec) {
     cg::cluster_group cluster = cg::this_cluster();
-    const int C = static_cast<int>(cluster.num_blocks());
-    const int crank = static_cast<int>(cluster.block_rank());
+    const int crank = C == 1 ? 0 : static_cast<int>(cluster.block_rank());
     const int64_t row = blockIdx.y;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -109,15 +109,25 @@ select_kernel(const float* __restrict__ scores, int64_t stride, int64_t tokens,
             const bool active = i < n;
             const uint32_t key = active ? key_at(i) : 0u;
             const bool want = active && (key & pmask) == prefix;
+            if (!__any_sync(0xffffffffu, want)) continue;
             const uint32_t digit = (key >> shift) & dmask;
             const unsigned peers = __match_any_sync(0xffffffffu, want ? digit : 0xffffffffu);
             if (want && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
         }
-        cluster.sync();
-        for (int bin = tid; bin < kBins; bin += kSelThreads) {
-            uint32_t s = 0u;
-            for (int r = 0; r < C; ++r) s += cluster.map_shared_rank(hist, r)[bin];
-            sh.total[bin] = s;
+        if constexpr (C == 1) {
+            __syncthreads();
+            for (int bin = tid; bin < kBins; bin += kSelThreads) sh.total[bin] = hist[bin];
+        } else {
+            cluster.sync();
+            for (int bin = tid; bin < kBins; bin += kSelThreads) {
+                uint32_t part[C];
+#pragma unroll
+                for (int r = 0; r < C; ++r) part[r] = cluster.map_shared_rank(hist, r)[bin];
+                uint32_t s = 0u;
+#pragma unroll
+                for (int r = 0; r < C; ++r) s += part[r];
+                sh.total[bin] = s;
+            }
         }
         __syncthreads();
         // Threshold digit: the bin where the count from the top first reaches `remaining`.
@@ -177,7 +187,7 @@ select_kernel(const float* __restrict__ scores, int64_t stride, int64_t tokens,
         sh.cta_gt = a;
         sh.cta_eq = b;
     }
-    cluster.sync();
+    if constexpr (C == 1) __syncthreads(); else cluster.sync();
     if (tid == 0) {
         uint32_t a = 0u, b = 0u;
         for (int r = 0; r < crank; ++r) {
@@ -211,7 +221,7 @@ select_kernel(const float* __restrict__ scores, int64_t stride, int64_t tokens,
         if (tid == 0) out[k] = static_cast<int32_t>(L);
         for (int64_t j = k + 1 + tid; j < budget; j += kSelThreads) out[j] = -1;
     }
-    cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+    if constexpr (C > 1) cluster.sync();  // keep shared memory alive until every peer has read it
 }
 
 }  // namespace
@@ -233,41 +243,42 @@ extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_str
         return fail(POPKV_ERR_INVALID_ARGUMENT, "rows_per_seq must be positive");
     if (rows == 0) return POPKV_OK;
     if (!indices || (tokens > 0 && !scores)) return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
-    // Cluster size: enough CTAs to fill the GPU, at least 1024 keys each, <= 8.
-    int64_t want = (tokens + kResidentMax - 1) / kResidentMax;
-    const int64_t fill = (296 + rows - 1) / rows;
-    if (fill > want) want = fill;
-    const int64_t by_size = (tokens + 1023) / 1024;
-    if (want > by_size) want = by_size;
+    // Cluster size: the smallest power of two (<= 8) whose per-CTA slice fits in
+    // shared memory; longer rows use 8 CTAs re-reading their slice from L2.
     int C = 1;
-    while (C < want && C < 8) C <<= 1;
+    while (C < 8 && (tokens + C - 1) / C > kResidentMax) C <<= 1;
     const int64_t chunk = (((tokens + C - 1) / C) + 3) / 4 * 4;
     const bool resident = chunk <= kResidentMax;
     const bool vec = aligned(scores, 16) && score_stride % 4 == 0;
     const size_t smem = resident ? (size_t)chunk * sizeof(uint32_t) : 0;
-
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)C, (unsigned)rows, 1);
-    cfg.blockDim = dim3(kSelThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = as_stream(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     const int64_t rps = rows_per_seq > 0 ? rows_per_seq : rows;
-    cudaError_t e;
-    if (resident) {
-        auto kern = select_kernel<true>;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaSuccess;
+    auto launch = [&](auto kern, int cluster) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)cluster, (unsigned)rows, 1);
+        cfg.blockDim = dim3(kSelThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = as_stream(stream);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (smem > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         e = cudaLaunchKernelEx(&cfg, kern, scores, score_stride, tokens, seq_len, rps, budget,
                                indices, vec);
+    };
+    if (resident) {
+        switch (C) {
+            case 1: launch(select_kernel<true, 1>, 1); break;
+            case 2: launch(select_kernel<true, 2>, 2); break;
+            case 4: launch(select_kernel<true, 4>, 4); break;
+            default: launch(select_kernel<true, 8>, 8); break;
+        }
     } else {
-        e = cudaLaunchKernelEx(&cfg, select_kernel<false>, scores, score_stride, tokens, seq_len,
-                               rps, budget, indices, vec);
+        launch(select_kernel<false, 8>, 8);
     }
     if (e != cudaSuccess) return fail(POPKV_ERR_CUDA, "popkv_select launch: %s", cudaGetErrorString(e));
     return check_launch("popkv_select");

@@ -10,8 +10,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
 #include <mutex>
-#include <unordered_map>
+#include <vector>
 
 #include "popkv_b200.h"
 
@@ -206,11 +207,14 @@ at::Tensor select_topk(const at::Tensor& scores, int64_t budget, int64_t tokens,
 }
 
 std::mutex g_ws_mutex;
-std::unordered_map<int, at::Tensor> g_workspaces;
+std::map<std::vector<int64_t>, at::Tensor> g_workspaces;
 
-at::Tensor default_workspace(const at::Device& dev, size_t bytes) {
+// One zero-initialised workspace per (device, shape) layout: the kernels keep a
+// workspace clean for the layout it was used with, not for a different one.
+at::Tensor default_workspace(const at::Device& dev, std::vector<int64_t> key, size_t bytes) {
     std::lock_guard<std::mutex> lock(g_ws_mutex);
-    auto& ws = g_workspaces[dev.index()];
+    key.push_back(dev.index());
+    auto& ws = g_workspaces[key];
     if (!ws.defined() || (size_t)ws.numel() < bytes)
         ws = at::zeros({(int64_t)bytes}, at::TensorOptions().device(dev).dtype(at::kByte));
     return ws;
@@ -279,7 +283,7 @@ at::Tensor sparse_attention(const at::Tensor& queries, const at::Tensor& key_cac
         CHECK_CUDA(ws); CHECK_CONTIGUOUS(ws);
         TORCH_CHECK((size_t)ws.nbytes() >= need, "workspace too small: ", ws.nbytes(), " < ", need);
     } else {
-        ws = default_workspace(queries.device(), need);
+        ws = default_workspace(queries.device(), {batch, q_heads, kv_heads, dim, tokens, splits}, need);
     }
     at::Tensor o = out ? *out : at::empty_like(queries);
     if (out) {

@@ -140,8 +140,10 @@ int popkv_select(const float* scores, int64_t rows, int64_t score_stride, int64_
  * the output of popkv_select.  indices == NULL selects dense attention over 0..L.
  * Scale 1/sqrt(head_dim), softmax and accumulation in fp32.
  * workspace: device buffer of popkv_sparse_attention_workspace_bytes(); it must be
- * zero-filled once after allocation (every call leaves it zeroed where it must be).
- * Calls that share a workspace must not overlap on the GPU.
+ * zero-filled once after allocation, and again before it is used with other
+ * (batch, q_heads, kv_heads, head_dim, tokens, splits): every call leaves it ready
+ * for the next call of the same sizes.  Calls that share a workspace must not
+ * overlap on the GPU.
  * splits: number of token segments per (sequence, KV head); 0 = automatic.
  */
 size_t popkv_sparse_attention_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,

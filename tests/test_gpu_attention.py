@@ -72,9 +72,20 @@ def test_attention_per_batch_caches_and_lengths():
     _case(3, 2, 8, 128, 2000, 256, torch.bfloat16, seed=3, per_batch=True, lengths=[2000, 17, 999])
 
 
-@pytest.mark.parametrize("splits", [1, 3, 64])
-def test_attention_explicit_splits(splits):
-    _case(1, 2, 8, 128, 4000, 512, torch.bfloat16, seed=splits, splits=splits)
+@pytest.mark.parametrize("splits,L", [(1, 2000), (3, 4000), (64, 4000)])
+def test_attention_explicit_splits(splits, L):
+    _case(1, 2, 8, 128, L, 512, torch.bfloat16, seed=splits, splits=splits)
+
+
+def test_attention_rejects_overlong_segments():
+    with pytest.raises(RuntimeError, match="segment longer"):
+        _case(1, 2, 8, 128, 4000, 512, torch.bfloat16, seed=0, splits=1)
+
+
+def test_attention_shape_changes_with_default_workspace():
+    """Alternating sizes on the shared default workspace stay correct."""
+    for L in (700, 3000, 700, 4096, 1500):
+        _case(1, 2, 8, 128, L, 256, torch.bfloat16, seed=L)
 
 
 def test_attention_workspace_reuse_is_clean():
