@@ -22,6 +22,7 @@
 // fp32 caches and head_dim outside {64, 96, 128} take a SIMT variant of the same
 // segment kernel.
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -765,4 +766,71 @@ extern "C" int popkv_sparse_attention(const void* queries, int dtype, int64_t ba
         return launch_simt<__half>(p, st);
     }
     return launch_simt<float>(p, st);
+}
+
+// ----------------------------------------------------------------------------
+// Allocation-free variant of popkv_sparse_attention.
+//
+// Some callers cannot allocate device memory at all: plugins that run inside a
+// host engine owning every allocation through its own pool, code paths that must
+// not call cudaMalloc while the engine holds its allocator lock, or embedders with
+// no allocator they may call.  For them this entry point takes its scratch from a
+// fixed array compiled into the library instead of a caller workspace.  The array
+// lives in every GPU that loads the library until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = POPKV_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once per
+// device (the host-side symbol is not a device address).
+int noalloc_scratch(void** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(POPKV_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(POPKV_ERR_UNSUPPORTED, "device index %d", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(POPKV_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = ptr;
+    }
+    *out = g_noalloc_ptr[dev];
+    return POPKV_OK;
+}
+
+}  // namespace
+
+extern "C" int popkv_sparse_attention_noalloc(
+    const void* queries, int dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* key_cache, const void* value_cache, int64_t kv_heads, int64_t kv_capacity,
+    int cache_per_batch, const void* current_keys, const void* current_values,
+    const int32_t* indices, int64_t index_stride, int64_t budget, int64_t tokens,
+    const int32_t* seq_len, void* out, int64_t splits, popkv_stream_t stream) {
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || tokens < 0)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "invalid attention shape");
+    const int64_t S = splits > 0 ? splits : auto_splits(batch, kv_heads, tokens);
+    const WorkspaceLayout w = layout(batch, q_heads, kv_heads, head_dim, tokens, S);
+    if (w.total > kNoAllocScratchBytes)
+        return fail(POPKV_ERR_WORKSPACE,
+                    "popkv_sparse_attention_noalloc needs %zu bytes of scratch for these sizes; "
+                    "its fixed scratch holds %zu (use popkv_sparse_attention with a workspace)",
+                    w.total, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc != POPKV_OK) return rc;
+    // The tickets and head masks must start at zero; the array keeps whatever the
+    // previous call (of any sizes) left there.
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, w.m, as_stream(stream));
+    if (e != cudaSuccess) return fail(POPKV_ERR_CUDA, "clearing scratch: %s", cudaGetErrorString(e));
+    return popkv_sparse_attention(queries, dtype, batch, q_heads, head_dim, key_cache, value_cache,
+                                  kv_heads, kv_capacity, cache_per_batch, current_keys,
+                                  current_values, indices, index_stride, budget, tokens, seq_len,
+                                  out, scratch, kNoAllocScratchBytes, S, stream);
 }

@@ -156,6 +156,31 @@ int popkv_sparse_attention(const void* queries, int dtype, int64_t batch, int64_
                            int64_t tokens, const int32_t* seq_len, void* out, void* workspace,
                            size_t workspace_bytes, int64_t splits, popkv_stream_t stream);
 
+/*
+ * Allocation-free variant of popkv_sparse_attention (no counterpart in the
+ * reference).  For callers that may not allocate device memory -- a plugin whose
+ * host engine owns every allocation, or code that must not call cudaMalloc while
+ * the engine holds its allocator -- the scratch comes from a fixed array of
+ * POPKV_NOALLOC_SCRATCH_BYTES built into the library (held on every GPU that
+ * loads it, until exit) instead of a caller workspace.  Arguments as for
+ * popkv_sparse_attention, minus the workspace.  Sizes whose scratch exceeds the
+ * array are rejected with POPKV_ERR_WORKSPACE (about 1.2 MB covers one
+ * Llama-3.1-8B layer at 32K tokens).  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) and should come before any stream
+ * capture.  Every call clears the parts that must start at zero; all calls share
+ * the one array, so calls that overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller.
+ */
+#define POPKV_NOALLOC_SCRATCH_BYTES (8u << 20)
+int popkv_sparse_attention_noalloc(const void* queries, int dtype, int64_t batch, int64_t q_heads,
+                                   int64_t head_dim, const void* key_cache,
+                                   const void* value_cache, int64_t kv_heads,
+                                   int64_t kv_capacity, int cache_per_batch,
+                                   const void* current_keys, const void* current_values,
+                                   const int32_t* indices, int64_t index_stride, int64_t budget,
+                                   int64_t tokens, const int32_t* seq_len, void* out,
+                                   int64_t splits, popkv_stream_t stream);
+
 /* Adds `increment` to seq_len[0..batch-1] on the device (end of a decode step). */
 int popkv_advance(int32_t* seq_len, int64_t batch, int32_t increment, popkv_stream_t stream);
 
