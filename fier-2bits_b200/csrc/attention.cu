@@ -16,9 +16,8 @@
 //  * each warp runs a flash-decoding tile of 16 rows on the tensor cores
 //    (mma.m16n8k16, bf16/fp16 in, fp32 accumulate) with the query heads packed
 //    into the M dimension, masking every (head, row) pair the head did not select;
-//  * partial (max, sum, acc) per (head, segment) go to the workspace and the last
-//    CTA of a (sequence, KV head) -- found with an atomic ticket, no spinning --
-//    combines them and resets its ticket.
+//  * partial (max, sum, acc) per (head, segment) go to the workspace and a
+//    combine kernel (one CTA per query head) merges them.
 // fp32 caches and head_dim outside {64, 96, 128} take a SIMT variant of the same
 // segment kernel.
 #include <cmath>
@@ -61,6 +60,7 @@ struct AttnParams {
     int S;
     float sl2;       // 1/sqrt(D) * log2(e)
     int work_bytes;  // scratch bytes before the token list (SIMT kernel)
+    int dense;       // attend every token 0..L (no head masks)
 };
 
 __device__ __forceinline__ int64_t seq_length(const AttnParams& p, int b) {
@@ -161,49 +161,42 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
     return total;
 }
 
-// -------------------------------------------------- completion and combine
-// Called by every thread after this CTA's partials are stored.  The last CTA of
-// (b, kvh) merges the S partials of its G heads into the output.
+// ----------------------------------------------------------------- combine
+// One CTA per (sequence, query head): merges the S segment partials (max, sum,
+// acc) into the output.  All S loads of a channel are independent, so the merge
+// costs a few L2 round trips.
 template <typename T>
-__device__ void finish_and_combine(const AttnParams& p, int b, int kvh, float* s_w, float* s_l) {
-    __shared__ int s_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(p.tickets + b * p.KVH + kvh, 1u);
-        s_last = prev == static_cast<uint32_t>(p.S - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+__global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
+    __shared__ float s_w[kMaxSplits];
+    __shared__ float s_red[2][4];
+    const int64_t row = blockIdx.x;  // b*QH + qh
     const int S = p.S;
-    const int64_t row0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
-    for (int i = threadIdx.x; i < p.G * S; i += blockDim.x) {
-        s_w[i] = __ldcg(p.ws_m + row0 * S + i);
-        s_l[i] = __ldcg(p.ws_l + row0 * S + i);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float mx = -INFINITY;
+    for (int s = tid; s < S; s += blockDim.x) {
+        s_w[s] = __ldcg(p.ws_m + row * S + s);
+        mx = fmaxf(mx, s_w[s]);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[0][warp] = mx;
     __syncthreads();
-    for (int h = threadIdx.x; h < p.G; h += blockDim.x) {
-        float M = -INFINITY;
-        for (int s = 0; s < S; ++s) M = fmaxf(M, s_w[h * S + s]);
-        float lsum = 0.0f;
-        for (int s = 0; s < S; ++s) {
-            const float m = s_w[h * S + s];
-            const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
-            s_w[h * S + s] = w;
-            lsum += w * s_l[h * S + s];
-        }
-        s_l[h * S] = 1.0f / lsum;  // s_l row h, slot 0 now holds 1/L
+    const float M = fmaxf(fmaxf(s_red[0][0], s_red[0][1]), fmaxf(s_red[0][2], s_red[0][3]));
+    float lsum = 0.0f;
+    for (int s = tid; s < S; s += blockDim.x) {
+        const float m = s_w[s];
+        const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
+        s_w[s] = w;
+        lsum += w * __ldcg(p.ws_l + row * S + s);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) s_red[1][warp] = lsum;
     __syncthreads();
-    // Every (head, channel) output sums S partials: issue the loads 8 at a time so
-    // the L2 latency overlaps (empty segments carry weight 0 and zero partials).
+    const float inv = 1.0f / (s_red[1][0] + s_red[1][1] + s_red[1][2] + s_red[1][3]);
     T* out = static_cast<T*>(p.out);
-    for (int i = threadIdx.x; i < p.G * p.D; i += blockDim.x) {
-        const int h = i / p.D;
-        const int d = i - h * p.D;
-        const float* acc = p.ws_acc + (row0 + h) * S * p.D + d;
-        const float* w = s_w + h * S;
+    for (int d = tid; d < p.D; d += blockDim.x) {
+        const float* acc = p.ws_acc + row * S * p.D + d;
         float o0 = 0.0f, o1 = 0.0f;
         int s = 0;
         for (; s + 8 <= S; s += 8) {
@@ -212,14 +205,13 @@ __device__ void finish_and_combine(const AttnParams& p, int b, int kvh, float* s
             for (int j = 0; j < 8; ++j) a[j] = __ldcg(acc + static_cast<int64_t>(s + j) * p.D);
 #pragma unroll
             for (int j = 0; j < 8; j += 2) {
-                o0 = fmaf(w[s + j], a[j], o0);
-                o1 = fmaf(w[s + j + 1], a[j + 1], o1);
+                o0 = fmaf(s_w[s + j], a[j], o0);
+                o1 = fmaf(s_w[s + j + 1], a[j + 1], o1);
             }
         }
-        for (; s < S; ++s) o0 = fmaf(w[s], __ldcg(acc + static_cast<int64_t>(s) * p.D), o0);
-        out[(row0 + h) * p.D + d] = from_float<T>((o0 + o1) * s_l[h * S]);
+        for (; s < S; ++s) o0 = fmaf(s_w[s], __ldcg(acc + static_cast<int64_t>(s) * p.D), o0);
+        out[row * p.D + d] = from_float<T>((o0 + o1) * inv);
     }
-    if (threadIdx.x == 0) p.tickets[b * p.KVH + kvh] = 0u;
 }
 
 // -------------------------------------------------------------- PTX helpers
@@ -312,7 +304,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
     const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
     const int64_t hi = imin64(lo + seg, L + 1);
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
-                                    p.indices == nullptr);
+                                    p.dense != 0);
 
     const T* q = static_cast<const T*>(p.q);
     const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
@@ -513,8 +505,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
         }
     }
     __syncthreads();
-    finish_and_combine<T>(p, b, kvh, reinterpret_cast<float*>(work),
-                          reinterpret_cast<float*>(work) + kMaxGroup * p.S);
 }
 
 // SIMT variant (fp32 caches, or head_dim outside the tensor-core instances).
@@ -541,7 +531,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_simt_kernel(AttnParams
     const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
     const int64_t hi = imin64(lo + seg, L + 1);
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
-                                    p.indices == nullptr);
+                                    p.dense != 0);
     const T* q = static_cast<const T*>(p.q);
     const T* kc = static_cast<const T*>(p.kc);
     const T* vc = static_cast<const T*>(p.vc);
@@ -616,8 +606,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_simt_kernel(AttnParams
         }
         __syncthreads();
     }
-    finish_and_combine<T>(p, b, kvh, reinterpret_cast<float*>(smem),
-                          reinterpret_cast<float*>(smem) + kMaxGroup * p.S);
 }
 
 struct WorkspaceLayout {
@@ -652,28 +640,30 @@ int64_t auto_splits(int64_t B, int64_t KVH, int64_t tokens) {
 template <typename T, int D>
 int launch_mma(const AttnParams& p, cudaStream_t st) {
     using Plan = MmaPlan<T, D>;
-    // The combine scratch (2 x 16 x S floats) reuses the copy ring.
-    const size_t combine = (size_t)2 * kMaxGroup * p.S * 4;
-    const size_t smem = (Plan::kWorkBytes > combine ? (size_t)Plan::kWorkBytes : combine) +
-                        Plan::kListBytes;
+    const size_t smem = (size_t)Plan::kWorkBytes + Plan::kListBytes;
     if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
     auto kern = attention_mma_kernel<T, D>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), kAttnThreads, smem, st>>>(p);
-    return check_launch("popkv_sparse_attention");
+    const int rc = check_launch("popkv_sparse_attention");
+    if (rc != POPKV_OK) return rc;
+    combine_kernel<T><<<(unsigned)(p.B * p.QH), 128, 0, st>>>(p);
+    return check_launch("popkv_sparse_attention (combine)");
 }
 
 template <typename T>
 int launch_simt(AttnParams p, cudaStream_t st) {
-    const int combine = 2 * kMaxGroup * p.S * 4;
     const int merge = (2 * kAttnWarps + kAttnWarps * p.D) * 4;
-    p.work_bytes = (combine > merge ? combine : merge + 15) / 16 * 16;
+    p.work_bytes = (merge + 15) / 16 * 16;
     const size_t smem = (size_t)p.work_bytes + kSegMax * 6;
     if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
     auto kern = attention_simt_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), kAttnThreads, smem, st>>>(p);
-    return check_launch("popkv_sparse_attention");
+    const int rc = check_launch("popkv_sparse_attention");
+    if (rc != POPKV_OK) return rc;
+    combine_kernel<T><<<(unsigned)(p.B * p.QH), 128, 0, st>>>(p);
+    return check_launch("popkv_sparse_attention (combine)");
 }
 
 }  // namespace
@@ -689,15 +679,16 @@ extern "C" size_t popkv_sparse_attention_workspace_bytes(int64_t batch, int64_t 
     return layout(batch, q_heads, kv_heads, head_dim, tokens, S).total;
 }
 
-extern "C" int popkv_sparse_attention(const void* queries, int dtype, int64_t batch,
-                                      int64_t q_heads, int64_t head_dim, const void* key_cache,
-                                      const void* value_cache, int64_t kv_heads,
-                                      int64_t kv_capacity, int cache_per_batch,
-                                      const void* current_keys, const void* current_values,
-                                      const int32_t* indices, int64_t index_stride,
-                                      int64_t budget, int64_t tokens, const int32_t* seq_len,
-                                      void* out, void* workspace, size_t workspace_bytes,
-                                      int64_t splits, popkv_stream_t stream) {
+enum AttnMode { kFromIndices = 0, kDense = 1, kPremasked = 2 };
+
+static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t q_heads,
+                          int64_t head_dim, const void* key_cache, const void* value_cache,
+                          int64_t kv_heads, int64_t kv_capacity, int cache_per_batch,
+                          const void* current_keys, const void* current_values,
+                          const int32_t* indices, int64_t index_stride, int64_t budget,
+                          int64_t tokens, const int32_t* seq_len, void* out, void* workspace,
+                          size_t workspace_bytes, int64_t splits, popkv_stream_t stream,
+                          int mode) {
     const size_t es = dtype_size(dtype);
     if (es == 0) return fail(POPKV_ERR_UNSUPPORTED, "dtype %d is not fp32/fp16/bf16", dtype);
     if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0)
@@ -744,9 +735,10 @@ extern "C" int popkv_sparse_attention(const void* queries, int dtype, int64_t ba
     p.tokens = tokens; p.seq_len = seq_len; p.S = (int)S;
     p.sl2 = (float)((1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634);
     p.work_bytes = 0;
+    p.dense = mode == kDense;
     const cudaStream_t st = as_stream(stream);
 
-    if (indices != nullptr) {
+    if (mode == kFromIndices) {
         const int64_t per_row = (budget < tokens + 1 ? budget : tokens + 1);
         const dim3 grid((unsigned)((per_row + 255) / 256), (unsigned)(batch * q_heads));
         scatter_kernel<<<grid, 256, 0, st>>>(p);
@@ -766,6 +758,47 @@ extern "C" int popkv_sparse_attention(const void* queries, int dtype, int64_t ba
         return launch_simt<__half>(p, st);
     }
     return launch_simt<float>(p, st);
+}
+
+extern "C" int popkv_sparse_attention(const void* queries, int dtype, int64_t batch,
+                                      int64_t q_heads, int64_t head_dim, const void* key_cache,
+                                      const void* value_cache, int64_t kv_heads,
+                                      int64_t kv_capacity, int cache_per_batch,
+                                      const void* current_keys, const void* current_values,
+                                      const int32_t* indices, int64_t index_stride,
+                                      int64_t budget, int64_t tokens, const int32_t* seq_len,
+                                      void* out, void* workspace, size_t workspace_bytes,
+                                      int64_t splits, popkv_stream_t stream) {
+    return attention_impl(queries, dtype, batch, q_heads, head_dim, key_cache, value_cache,
+                          kv_heads, kv_capacity, cache_per_batch, current_keys, current_values,
+                          indices, index_stride, budget, tokens, seq_len, out, workspace,
+                          workspace_bytes, splits, stream, indices ? kFromIndices : kDense);
+}
+
+extern "C" int popkv_sparse_attention_premasked(
+    const void* queries, int dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* key_cache, const void* value_cache, int64_t kv_heads, int64_t kv_capacity,
+    int cache_per_batch, const void* current_keys, const void* current_values, int64_t tokens,
+    const int32_t* seq_len, void* out, void* workspace, size_t workspace_bytes, int64_t splits,
+    popkv_stream_t stream) {
+    return attention_impl(queries, dtype, batch, q_heads, head_dim, key_cache, value_cache,
+                          kv_heads, kv_capacity, cache_per_batch, current_keys, current_values,
+                          nullptr, 0, 2, tokens, seq_len, out, workspace, workspace_bytes, splits,
+                          stream, kPremasked);
+}
+
+extern "C" int popkv_sparse_attention_masks(void* workspace, int64_t batch, int64_t q_heads,
+                                            int64_t kv_heads, int64_t head_dim, int64_t tokens,
+                                            int64_t splits, uint16_t** masks,
+                                            int64_t* mask_stride) {
+    if (!workspace || !masks || !mask_stride) return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
+    if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || tokens < 0)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "invalid attention shape");
+    const int64_t S = splits > 0 ? splits : auto_splits(batch, kv_heads, tokens);
+    const WorkspaceLayout w = layout(batch, q_heads, kv_heads, head_dim, tokens, S);
+    *masks = reinterpret_cast<uint16_t*>(static_cast<unsigned char*>(workspace) + w.masks);
+    *mask_stride = w.mask_stride;
+    return POPKV_OK;
 }
 
 // ----------------------------------------------------------------------------

@@ -25,6 +25,14 @@ namespace {
 constexpr int kScoreThreads = 256;
 constexpr int kTokensPerThread = 2;
 constexpr int kTile = kScoreThreads * kTokensPerThread;
+constexpr int kBins = 2048;     // histogram of the top 11 bits of each score's order key
+constexpr int kHistHeads = 8;   // query heads per KV head covered by the in-CTA histogram
+
+// Exact float of a small integer (|n| < 2^22) with two full-rate ALU operations:
+// 1.5 * 2^23 + n has n in its low mantissa bits, and subtracting 1.5 * 2^23 is exact.
+__device__ __forceinline__ float small_int_to_float(int n) {
+    return __fsub_rn(__int_as_float(0x4B400000 + n), 12582912.0f);
+}
 
 template <int W, bool VEC>
 struct PackedRow {
@@ -77,9 +85,11 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
              int kv_heads, int64_t capacity, bool per_batch,
              const int64_t* __restrict__ head_to_kv, int64_t tokens,
              const int32_t* __restrict__ seq_len, float* __restrict__ scores, int64_t stride,
-             float scale, bool ref_div) {
+             float scale, bool ref_div, uint32_t* __restrict__ score_hist, int hist_heads) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    int* s_heads = reinterpret_cast<int*>(smem_raw);                 // [q_heads]
+    uint32_t* s_hist = reinterpret_cast<uint32_t*>(smem_raw);         // [hist_heads][kBins]
+    float* s_abs = reinterpret_cast<float*>(s_hist + hist_heads * kBins);  // [warps][W*32]
+    int* s_heads = reinterpret_cast<int*>(s_abs + (kScoreThreads / 32) * W * 32);  // [q_heads]
     uint32_t* s_qs = reinterpret_cast<uint32_t*>(s_heads + q_heads);  // [q_heads][W]
     uint32_t* s_qm = s_qs + q_heads * W;
     float* s_ql = reinterpret_cast<float*>(s_qm + q_heads * W);
@@ -119,8 +129,13 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
     }
     __syncthreads();
     const int nh = s_nh;
+    const bool use_hist = score_hist != nullptr && nh <= hist_heads;
 
-    // 3. Warp-parallel query pack, one warp per query head.
+    // 3. Warp-parallel query pack, one warp per query head: ballots give the bit
+    // words; lane j then sums word j's magnitudes in channel order from shared memory.
+    if (use_hist)
+        for (int i = tid; i < nh * kBins; i += kScoreThreads) s_hist[i] = 0u;
+    float* my_abs = s_abs + warp * (W * 32);
     for (int slot = warp; slot < nh; slot += kScoreThreads / 32) {
         const TQ* q = queries + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * D;
         float v[W];
@@ -130,6 +145,7 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
             const int c = 32 * j + lane;
             v[j] = c < D ? to_float<TQ>(q[c]) : 0.0f;
             if (c < D) { mn = fminf(mn, v[j]); mx = fmaxf(mx, v[j]); }
+            my_abs[32 * j + lane] = fabsf(v[j]);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -147,20 +163,16 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
             const uint32_t mw = __ballot_sync(0xffffffffu, mg);
             if (lane == j) { my_sw = sw; my_mw = mw; }
         }
-        // Channel-order sums: lane j accumulates word j.
-        float ls = 0.0f, hs = 0.0f;
-        int lc = 0, hc = 0;
-        for (int i = 0; i < 32; ++i) {
-#pragma unroll
-            for (int j = 0; j < W; ++j) {
-                const float x = __shfl_sync(0xffffffffu, v[j], i);
-                if (lane == j && 32 * j + i < D) {
-                    if ((my_mw >> i) & 1u) { hs += fabsf(x); ++hc; }
-                    else { ls += fabsf(x); ++lc; }
-                }
-            }
-        }
+        __syncwarp();
         if (lane < W) {
+            float ls = 0.0f, hs = 0.0f;
+            int lc = 0, hc = 0;
+            const int n = min(32, D - 32 * lane);
+            for (int i = 0; i < n; ++i) {
+                const float x = my_abs[32 * lane + i];
+                if ((my_mw >> i) & 1u) { hs += x; ++hc; }
+                else { ls += x; ++lc; }
+            }
             float low, high;
             representatives(ls, lc, hs, hc, ref_div, low, high);
             s_qs[slot * W + lane] = my_sw;
@@ -168,6 +180,7 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
             s_ql[slot * W + lane] = low;
             s_qd[slot * W + lane] = high - low;
         }
+        __syncwarp();
     }
     __syncthreads();
 
@@ -175,6 +188,19 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
     const float sc = ref_div ? rsqrtf(static_cast<float>(D)) : scale;
     for (int slot = 0; slot < nh; ++slot) {
         float* out = scores + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * stride;
+        uint32_t* hist = s_hist + slot * kBins;
+        uint32_t qs[W], qm[W];
+        float ql[W], dq[W];
+        int pq[W];
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+            const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
+            qs[w] = s_qs[slot * W + w];
+            qm[w] = s_qm[slot * W + w] & valid;
+            ql[w] = s_ql[slot * W + w];
+            dq[w] = s_qd[slot * W + w];
+            pq[w] = __popc(qm[w]);
+        }
 #pragma unroll
         for (int j = 0; j < kTokensPerThread; ++j) {
             const int64_t t = t_base + j * kScoreThreads + tid;
@@ -183,25 +209,32 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
 #pragma unroll
             for (int w = 0; w < W; ++w) {
                 const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
-                const uint32_t qs = s_qs[slot * W + w];
-                const uint32_t qm = s_qm[slot * W + w] & valid;
                 const uint32_t km = rows[j].m[w] & valid;
-                const uint32_t match = ~(qs ^ rows[j].s[w]) & valid;
-                const uint32_t both = qm & km;
+                const uint32_t match = ~(qs[w] ^ rows[j].s[w]) & valid;
+                const uint32_t both = qm[w] & km;
                 const int cs = 2 * __popc(match) - __popc(valid);
-                const int cq = 2 * __popc(match & qm) - __popc(qm);
+                const int cq = 2 * __popc(match & qm[w]) - pq[w];
                 const int ck = 2 * __popc(match & km) - __popc(km);
                 const int cqk = 2 * __popc(match & both) - __popc(both);
-                const float ql = s_ql[slot * W + w], dq = s_qd[slot * W + w];
                 const float kl = __half2float(__ushort_as_half(rows[j].l[w]));
                 const float dk = __half2float(__ushort_as_half(rows[j].d[w]));
-                const float inner = __fmul_rn(__fmul_rn(dq, dk), static_cast<float>(cqk));
-                const float gs = fmaf(__fmul_rn(ql, kl), static_cast<float>(cs),
-                                      fmaf(__fmul_rn(dq, kl), static_cast<float>(cq),
-                                           fmaf(__fmul_rn(ql, dk), static_cast<float>(ck), inner)));
+                const float inner = __fmul_rn(__fmul_rn(dq[w], dk), small_int_to_float(cqk));
+                const float gs = fmaf(__fmul_rn(ql[w], kl), small_int_to_float(cs),
+                                      fmaf(__fmul_rn(dq[w], kl), small_int_to_float(cq),
+                                           fmaf(__fmul_rn(ql[w], dk), small_int_to_float(ck), inner)));
                 score = __fadd_rn(score, gs);
             }
-            out[t] = __fmul_rn(score, sc);
+            const float v = __fmul_rn(score, sc);
+            out[t] = v;
+            if (use_hist) atomicAdd(hist + (order_key(v) >> 21), 1u);
+        }
+    }
+    if (use_hist) {
+        __syncthreads();
+        for (int i = tid; i < nh * kBins; i += kScoreThreads) {
+            const uint32_t c = s_hist[i];
+            if (c) atomicAdd(score_hist + (static_cast<int64_t>(b) * q_heads + s_heads[i / kBins]) * kBins +
+                                 (i % kBins), c);
         }
     }
 }
@@ -211,15 +244,17 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
                    const int32_t* mg, const uint16_t* lo, const uint16_t* de, int64_t kv_heads,
                    int64_t cap, bool per_batch, const int64_t* h2k, int64_t tokens,
                    const int32_t* seq_len, float* scores, int64_t stride, float scale,
-                   bool ref_div, bool vec, cudaStream_t st) {
+                   bool ref_div, bool vec, uint32_t* hist, cudaStream_t st) {
     const dim3 grid((unsigned)((tokens + kTile - 1) / kTile), (unsigned)(batch * kv_heads));
-    const size_t smem = (size_t)q_heads * (sizeof(int) + (size_t)W * 16);
+    const int hist_heads = hist ? (int)(q_heads < kHistHeads ? q_heads : kHistHeads) : 0;
+    const size_t smem = (size_t)hist_heads * kBins * 4 + (size_t)(kScoreThreads / 32) * W * 32 * 4 +
+                        (size_t)q_heads * (sizeof(int) + (size_t)W * 16);
     auto run = [&](auto kern) {
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         kern<<<grid, kScoreThreads, smem, st>>>(
             static_cast<const TQ*>(q), (int)q_heads, D, sg, mg, lo, de, (int)kv_heads, cap,
-            per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div);
+            per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div, hist, hist_heads);
     };
     if (vec) run(score_kernel<TQ, W, true>);
     else run(score_kernel<TQ, W, false>);
@@ -251,7 +286,8 @@ extern "C" int popkv_score(const void* queries, int q_dtype, int64_t batch, int6
                            const uint16_t* low, const uint16_t* delta, int64_t kv_heads,
                            int64_t capacity, int cache_per_batch, const int64_t* head_to_kv,
                            int64_t tokens, const int32_t* seq_len, float* scores,
-                           int64_t score_stride, int flags, popkv_stream_t stream) {
+                           int64_t score_stride, uint32_t* score_hist, int flags,
+                           popkv_stream_t stream) {
     if (dtype_size(q_dtype) == 0)
         return fail(POPKV_ERR_UNSUPPORTED, "queries dtype %d is not fp32/fp16/bf16", q_dtype);
     if (batch < 0 || q_heads <= 0 || head_dim <= 0 || kv_heads <= 0)
@@ -277,15 +313,15 @@ extern "C" int popkv_score(const void* queries, int q_dtype, int64_t batch, int6
         case POPKV_F32:
             return score_words<float>(W, queries, batch, q_heads, (int)head_dim, k_sign, k_mag, low,
                                       delta, kv_heads, capacity, cache_per_batch != 0, head_to_kv,
-                                      tokens, seq_len, scores, score_stride, scale, ref_div, vec, st);
+                                      tokens, seq_len, scores, score_stride, scale, ref_div, vec, score_hist, st);
         case POPKV_F16:
             return score_words<__half>(W, queries, batch, q_heads, (int)head_dim, k_sign, k_mag, low,
                                        delta, kv_heads, capacity, cache_per_batch != 0, head_to_kv,
-                                       tokens, seq_len, scores, score_stride, scale, ref_div, vec, st);
+                                       tokens, seq_len, scores, score_stride, scale, ref_div, vec, score_hist, st);
         default:
             return score_words<__nv_bfloat16>(W, queries, batch, q_heads, (int)head_dim, k_sign,
                                               k_mag, low, delta, kv_heads, capacity,
                                               cache_per_batch != 0, head_to_kv, tokens, seq_len,
-                                              scores, score_stride, scale, ref_div, vec, st);
+                                              scores, score_stride, scale, ref_div, vec, score_hist, st);
     }
 }

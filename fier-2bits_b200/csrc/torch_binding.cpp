@@ -53,6 +53,13 @@ void check_packed(const std::vector<at::Tensor>& packed) {
                 "packed tensors are [KVH, capacity, words] or [B, KVH, capacity, words]");
 }
 
+uint32_t* hist_ptr(const c10::optional<at::Tensor>& hist, int64_t rows) {
+    if (!hist) return nullptr;
+    CHECK_CUDA(*hist); CHECK_CONTIGUOUS(*hist); CHECK_DTYPE(*hist, at::kInt);
+    TORCH_CHECK(hist->numel() == rows * 2048, "score histogram must be int32 [rows, 2048]");
+    return reinterpret_cast<uint32_t*>(hist->data_ptr<int32_t>());
+}
+
 std::vector<at::Tensor> pack(const at::Tensor& keys, int64_t token_capacity, int64_t flags,
                              bool with_thresholds) {
     CHECK_CUDA(keys); CHECK_CONTIGUOUS(keys);
@@ -142,7 +149,7 @@ void append(const at::Tensor& key_cache, const c10::optional<at::Tensor>& value_
 at::Tensor score(const at::Tensor& queries, const at::Tensor& k_sign, const at::Tensor& k_mag,
                  const at::Tensor& low, const at::Tensor& delta, const at::Tensor& head_to_kv,
                  int64_t tokens, int64_t flags, const c10::optional<at::Tensor>& seq_len,
-                 const c10::optional<at::Tensor>& out) {
+                 const c10::optional<at::Tensor>& out, const c10::optional<at::Tensor>& hist) {
     CHECK_CUDA(queries); CHECK_CONTIGUOUS(queries);
     TORCH_CHECK(queries.dim() == 3, "queries must be [B, QH, D]");
     check_packed({k_sign, k_mag, low, delta});
@@ -173,21 +180,22 @@ at::Tensor score(const at::Tensor& queries, const at::Tensor& k_sign, const at::
                                reinterpret_cast<const uint16_t*>(low.data_ptr<at::Half>()),
                                reinterpret_cast<const uint16_t*>(delta.data_ptr<at::Half>()),
                                kv_heads, cap, per_batch ? 1 : 0, head_to_kv.data_ptr<int64_t>(),
-                               tokens, sl, scores.data_ptr<float>(), scores.size(2), (int)flags,
-                               stream_of(queries));
+                               tokens, sl, scores.data_ptr<float>(), scores.size(2),
+                               hist_ptr(hist, batch * q_heads), (int)flags, stream_of(queries));
     check_status(rc, "popkv_score");
     return scores;
 }
 
 at::Tensor select_topk(const at::Tensor& scores, int64_t budget, int64_t tokens,
-                  const c10::optional<at::Tensor>& seq_len, int64_t rows_per_seq,
-                  const c10::optional<at::Tensor>& out) {
+                       const c10::optional<at::Tensor>& seq_len, int64_t rows_per_seq,
+                       const c10::optional<at::Tensor>& out,
+                       const c10::optional<at::Tensor>& attn_workspace,
+                       std::vector<int64_t> attn_sizes, const c10::optional<at::Tensor>& hist) {
     CHECK_CUDA(scores); CHECK_DTYPE(scores, at::kFloat);
     TORCH_CHECK(scores.stride(-1) == 1, "scores rows must be contiguous");
     const int64_t stride = scores.dim() > 1 ? scores.stride(-2) : scores.size(-1);
     const int64_t rows = scores.numel() / std::max<int64_t>(scores.size(-1), 1);
-    TORCH_CHECK(scores.dim() == 1 || scores.is_contiguous() || scores.dim() == 2,
-                "scores must be contiguous or a 2-D row view");
+    TORCH_CHECK(scores.dim() <= 2 || scores.is_contiguous(), "scores must be contiguous or a 2-D row view");
     TORCH_CHECK(tokens <= scores.size(-1), "tokens exceed the score row length");
     const int32_t* sl = nullptr;
     if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
@@ -200,8 +208,25 @@ at::Tensor select_topk(const at::Tensor& scores, int64_t budget, int64_t tokens,
     } else {
         idx = at::empty({rows, budget}, scores.options().dtype(at::kInt));
     }
+    uint16_t* masks = nullptr;
+    int64_t mask_stride = 0, heads_per_kv = 0;
+    if (attn_workspace) {
+        // attn_sizes = (batch, q_heads, kv_heads, head_dim, tokens, splits) of the attention call.
+        TORCH_CHECK(attn_sizes.size() == 6, "attn_sizes = (batch, q_heads, kv_heads, head_dim, tokens, splits)");
+        CHECK_CUDA(*attn_workspace); CHECK_CONTIGUOUS(*attn_workspace);
+        const size_t need = popkv_sparse_attention_workspace_bytes(attn_sizes[0], attn_sizes[1], attn_sizes[2],
+                                                                   attn_sizes[3], attn_sizes[4], attn_sizes[5]);
+        TORCH_CHECK((size_t)attn_workspace->nbytes() >= need, "attention workspace too small");
+        check_status(popkv_sparse_attention_masks(attn_workspace->data_ptr(), attn_sizes[0], attn_sizes[1],
+                                                  attn_sizes[2], attn_sizes[3], attn_sizes[4], attn_sizes[5],
+                                                  &masks, &mask_stride),
+                     "popkv_sparse_attention_masks");
+        heads_per_kv = attn_sizes[1] / attn_sizes[2];
+        TORCH_CHECK(rows_per_seq == attn_sizes[1], "rows_per_seq must equal q_heads with head masks");
+    }
     const int rc = popkv_select(scores.data_ptr<float>(), rows, stride, tokens, sl, rows_per_seq,
-                                budget, idx.data_ptr<int32_t>(), stream_of(scores));
+                                budget, idx.data_ptr<int32_t>(), masks, mask_stride, heads_per_kv,
+                                hist_ptr(hist, rows), stream_of(scores));
     check_status(rc, "popkv_select");
     return idx;
 }
@@ -299,6 +324,30 @@ at::Tensor sparse_attention(const at::Tensor& queries, const at::Tensor& key_cac
     return o;
 }
 
+at::Tensor sparse_attention_premasked(const at::Tensor& queries, const at::Tensor& key_cache,
+                                     const at::Tensor& value_cache, int64_t tokens,
+                                     const at::Tensor& current_keys, const at::Tensor& current_values,
+                                     const c10::optional<at::Tensor>& seq_len,
+                                     const at::Tensor& workspace, int64_t splits, const at::Tensor& out) {
+    for (const at::Tensor* t : {&queries, &key_cache, &value_cache, &current_keys, &current_values, &workspace, &out}) {
+        CHECK_CUDA(*t); CHECK_CONTIGUOUS(*t);
+    }
+    TORCH_CHECK(queries.dim() == 3 && out.sizes() == queries.sizes(), "queries/out must be [B, QH, D]");
+    TORCH_CHECK(key_cache.sizes() == value_cache.sizes() && key_cache.dim() == 4, "caches are [B, KVH, capacity, D]");
+    const int64_t batch = queries.size(0), q_heads = queries.size(1), dim = queries.size(2);
+    const int64_t kv_heads = key_cache.size(1);
+    const int32_t* sl = nullptr;
+    if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
+    c10::cuda::CUDAGuard guard(queries.device());
+    const int rc = popkv_sparse_attention_premasked(
+        queries.data_ptr(), dtype_code(queries), batch, q_heads, dim, key_cache.data_ptr(),
+        value_cache.data_ptr(), kv_heads, key_cache.size(2), 1, current_keys.data_ptr(),
+        current_values.data_ptr(), tokens, sl, out.data_ptr(), workspace.data_ptr(),
+        (size_t)workspace.nbytes(), splits, stream_of(queries));
+    check_status(rc, "popkv_sparse_attention_premasked");
+    return out;
+}
+
 void advance(const at::Tensor& seq_len, int64_t increment) {
     CHECK_CUDA(seq_len); CHECK_CONTIGUOUS(seq_len); CHECK_DTYPE(seq_len, at::kInt);
     c10::cuda::CUDAGuard guard(seq_len.device());
@@ -321,9 +370,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("kv_heads_per_seq") = 0, py::arg("flags") = 0);
     m.def("score", &score, py::arg("queries"), py::arg("k_sign"), py::arg("k_mag"), py::arg("low"),
           py::arg("delta"), py::arg("head_to_kv"), py::arg("tokens"), py::arg("flags") = 0,
-          py::arg("seq_len") = py::none(), py::arg("out") = py::none());
+          py::arg("seq_len") = py::none(), py::arg("out") = py::none(), py::arg("hist") = py::none());
     m.def("select", &select_topk, py::arg("scores"), py::arg("budget"), py::arg("tokens"),
-          py::arg("seq_len") = py::none(), py::arg("rows_per_seq") = 0, py::arg("out") = py::none());
+          py::arg("seq_len") = py::none(), py::arg("rows_per_seq") = 0, py::arg("out") = py::none(),
+          py::arg("attn_workspace") = py::none(), py::arg("attn_sizes") = std::vector<int64_t>{},
+          py::arg("hist") = py::none());
+    m.def("sparse_attention_premasked", &sparse_attention_premasked);
     m.def("sparse_attention", &sparse_attention, py::arg("queries"), py::arg("key_cache"),
           py::arg("value_cache"), py::arg("indices"), py::arg("budget"), py::arg("tokens"),
           py::arg("current_keys") = py::none(), py::arg("current_values") = py::none(),

@@ -202,6 +202,7 @@ class RetrievalStack:
                        for _ in range(layers)]
         self.head_to_kv = (torch.arange(QH, device=dev) // (QH // H)).to(torch.int64)
         self.scores = torch.empty(B, QH, self.capacity, dtype=torch.float32, device=dev)
+        self.score_hist = pk.new_score_histogram(B * QH, dev)
         self.indices = [torch.empty(B * QH, budget, dtype=torch.int32, device=dev) for _ in range(layers)]
         self.workspace = [pk.new_workspace(B, QH, H, head_dim, self.max_tokens, dev) for _ in range(layers)]
         self.seq_len = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -235,13 +236,15 @@ class RetrievalStack:
     def _layer(self, i: int) -> None:
         tokens = self.max_tokens
         pk.score(self.q_in[i], self.packed[i], head_to_kv=self.head_to_kv, tokens=tokens,
-                 seq_len=self.seq_len, out=self.scores)
+                 seq_len=self.seq_len, out=self.scores, hist=self.score_hist)
+        sizes = (self.batch, self.q_heads, self.kv_heads, self.head_dim, tokens, 0)
         pk.select(self.scores.view(-1, self.capacity), budget=self.budget, tokens=tokens,
-                  seq_len=self.seq_len, rows_per_seq=self.q_heads, out=self.indices[i])
-        pk.sparse_attention(self.q_in[i], self.key_cache[i], self.value_cache[i], self.indices[i],
-                            budget=self.budget, tokens=tokens, current_keys=self.k_in[i],
-                            current_values=self.v_in[i], seq_len=self.seq_len,
-                            workspace=self.workspace[i], out=self.out[i])
+                  seq_len=self.seq_len, rows_per_seq=self.q_heads, out=self.indices[i],
+                  attn_workspace=self.workspace[i], attn_sizes=sizes, hist=self.score_hist)
+        pk.sparse_attention_premasked(self.q_in[i], self.key_cache[i], self.value_cache[i],
+                                      tokens=tokens, current_keys=self.k_in[i],
+                                      current_values=self.v_in[i], seq_len=self.seq_len,
+                                      workspace=self.workspace[i], out=self.out[i])
         pk.append_keys(self.key_cache[i], self.value_cache[i], self.k_in[i], self.v_in[i],
                        self.packed[i], position=0, seq_len=self.seq_len,
                        kv_heads_per_seq=self.kv_heads)
@@ -283,5 +286,5 @@ class RetrievalStack:
         self.graph = g
 
     def launches_per_step(self) -> int:
-        # score, select, scatter + attention, append per layer, + advance.
+        # score, select, attention + combine, append per layer, + advance.
         return self.layers * 5 + 1

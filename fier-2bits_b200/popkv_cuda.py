@@ -57,16 +57,18 @@ def pack_keys_into(keys: torch.Tensor, packed, *, token_offset: int, flags: int 
 
 def score(queries: torch.Tensor, packed, *, head_to_kv: torch.Tensor, tokens: int,
           flags: int = 0, seq_len: torch.Tensor | None = None,
-          out: torch.Tensor | None = None) -> torch.Tensor:
+          out: torch.Tensor | None = None, hist: torch.Tensor | None = None) -> torch.Tensor:
     """Return Pop-KV approximate QK scores for every query head and token.
 
     queries [B, QH, D]; packed [KVH, cap, W] (shared by the batch, as in the
     reference) or [B, KVH, cap, W] (one cache per sequence) -> fp32 [B, QH, tokens].
+    ``hist`` (int32 [B*QH, 2048], zero) collects each row's top-11-bit key histogram
+    for ``select(hist=...)``, which consumes and re-zeroes it.
     """
     if queries.ndim != 3 or not queries.is_cuda or not queries.is_contiguous():
         raise ValueError("queries must be contiguous CUDA [batch, query heads, head dim]")
     return extension().score(queries, *_packed(packed), head_to_kv.contiguous(), int(tokens),
-                             int(flags), seq_len, out)
+                             int(flags), seq_len, out, hist)
 
 
 def append_keys(key_cache: torch.Tensor, value_cache: torch.Tensor | None, new_keys,
@@ -86,18 +88,34 @@ def append_keys(key_cache: torch.Tensor, value_cache: torch.Tensor | None, new_k
 
 def select(scores: torch.Tensor, *, budget: int, tokens: int | None = None,
            seq_len: torch.Tensor | None = None, rows_per_seq: int = 0,
-           out: torch.Tensor | None = None) -> torch.Tensor:
+           out: torch.Tensor | None = None, attn_workspace: torch.Tensor | None = None,
+           attn_sizes: tuple = (), hist: torch.Tensor | None = None) -> torch.Tensor:
     """Top-(budget-1) token indices per row plus the newest token.
 
     scores [..., L] fp32 -> int32 [rows, budget]: the min(budget-1, L) best tokens in
     ascending index order (ties to the lowest index), then L, then -1 padding.
+    With ``attn_workspace`` (and ``attn_sizes`` = (batch, q_heads, kv_heads, head_dim,
+    tokens, splits) of the attention call that will use it) the selection is also
+    written as the workspace's token bitmask for ``sparse_attention_premasked``.
     """
     if not scores.is_cuda or scores.dtype != torch.float32:
         raise ValueError("scores must be a CUDA float32 tensor")
     if int(budget) <= 1:
         raise ValueError("budget must reserve at least one retrieved and one current token")
     tokens = int(scores.shape[-1]) if tokens is None else int(tokens)
-    return extension().select(scores, int(budget), tokens, seq_len, int(rows_per_seq), out)
+    return extension().select(scores, int(budget), tokens, seq_len, int(rows_per_seq), out,
+                              attn_workspace, [int(x) for x in attn_sizes], hist)
+
+
+def sparse_attention_premasked(queries, key_cache, value_cache, *, tokens: int, current_keys,
+                               current_values, workspace, out, seq_len=None, splits: int = 0):
+    """sparse_attention over the bitmask that ``select(attn_workspace=workspace)`` wrote.
+
+    Batched caches [B, KVH, kv_cap, D]; queries/out [B, QH, D]; current rows [B, KVH, D].
+    """
+    return extension().sparse_attention_premasked(queries, key_cache, value_cache, int(tokens),
+                                                  current_keys, current_values, seq_len,
+                                                  workspace, int(splits), out)
 
 
 def sparse_attention(queries: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
@@ -122,6 +140,11 @@ def sparse_attention(queries: torch.Tensor, key_cache: torch.Tensor, value_cache
     return extension().sparse_attention(queries, key_cache, value_cache, indices, int(budget),
                                         int(tokens), current_keys, current_values, seq_len,
                                         workspace, int(splits), out)
+
+
+def new_score_histogram(rows: int, device) -> torch.Tensor:
+    """Zeroed int32 [rows, 2048] histogram shared by ``score`` and ``select``."""
+    return torch.zeros(rows, 2048, dtype=torch.int32, device=device)
 
 
 def workspace_bytes(batch: int, q_heads: int, kv_heads: int, head_dim: int, tokens: int,

@@ -104,13 +104,17 @@ int popkv_append(void* key_cache, void* value_cache, int dtype, int64_t heads,
  * queries: [batch, q_heads, head_dim] of q_dtype; head_to_kv: int64 [q_heads] (device).
  * scores: fp32 [batch, q_heads, score_stride]; tokens 0..L-1 of every row are written.
  * Requires tokens <= capacity and tokens <= score_stride.
+ * score_hist (nullable): uint32 [batch*q_heads, 2048], zero on entry; receives the
+ * count of each row's scores per value of the top 11 bits of their order key (a
+ * head of a KV head with more than 8 query heads is skipped).  popkv_select uses
+ * it to skip its threshold search and zeroes it again.
  */
 int popkv_score(const void* queries, int q_dtype, int64_t batch, int64_t q_heads,
                 int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
                 const uint16_t* low, const uint16_t* delta, int64_t kv_heads, int64_t capacity,
                 int cache_per_batch, const int64_t* head_to_kv, int64_t tokens,
-                const int32_t* seq_len, float* scores, int64_t score_stride, int flags,
-                popkv_stream_t stream);
+                const int32_t* seq_len, float* scores, int64_t score_stride,
+                uint32_t* score_hist, int flags, popkv_stream_t stream);
 
 /*
  * (e) Per-row top-(budget-1) with the newest token reserved.  Replaces
@@ -120,10 +124,17 @@ int popkv_score(const void* queries, int q_dtype, int64_t batch, int64_t q_heads
  * indices: int32 [rows, budget]: the k = min(budget-1, L) largest scores' token
  * indices in ascending index order (ties -> lowest index; -0.0 == +0.0), then L,
  * then -1 padding.
+ * head_masks (nullable): also OR the selection into the per-KV-head token bitmask
+ * of an attention workspace (see popkv_sparse_attention_masks): row r = b*QH + qh
+ * sets bit qh % heads_per_kv of token t in mask row b*(QH/heads_per_kv) + qh/heads_per_kv,
+ * with rows_per_seq = QH.  popkv_sparse_attention_premasked then skips its own scatter.
+ * score_hist (nullable): the histogram popkv_score wrote for these rows; used when
+ * its row total equals L (else ignored), and zeroed for the next step.
  */
 int popkv_select(const float* scores, int64_t rows, int64_t score_stride, int64_t tokens,
                  const int32_t* seq_len, int64_t rows_per_seq, int64_t budget,
-                 int32_t* indices, popkv_stream_t stream);
+                 int32_t* indices, uint16_t* head_masks, int64_t mask_stride,
+                 int64_t heads_per_kv, uint32_t* score_hist, popkv_stream_t stream);
 
 /*
  * (f) Fused gather + exact split-K decode attention.  Replaces gather_selected_kv +
@@ -155,6 +166,24 @@ int popkv_sparse_attention(const void* queries, int dtype, int64_t batch, int64_
                            const int32_t* indices, int64_t index_stride, int64_t budget,
                            int64_t tokens, const int32_t* seq_len, void* out, void* workspace,
                            size_t workspace_bytes, int64_t splits, popkv_stream_t stream);
+
+/*
+ * popkv_sparse_attention over the token bitmask already written into `workspace`
+ * by popkv_select(head_masks = popkv_sparse_attention_masks(workspace, ...)) for the
+ * same sizes; saves the scatter of the index lists.  Same arguments otherwise.
+ */
+int popkv_sparse_attention_premasked(const void* queries, int dtype, int64_t batch,
+                                     int64_t q_heads, int64_t head_dim, const void* key_cache,
+                                     const void* value_cache, int64_t kv_heads,
+                                     int64_t kv_capacity, int cache_per_batch,
+                                     const void* current_keys, const void* current_values,
+                                     int64_t tokens, const int32_t* seq_len, void* out,
+                                     void* workspace, size_t workspace_bytes, int64_t splits,
+                                     popkv_stream_t stream);
+/* Token-bitmask region of an attention workspace (for popkv_select's head_masks). */
+int popkv_sparse_attention_masks(void* workspace, int64_t batch, int64_t q_heads,
+                                 int64_t kv_heads, int64_t head_dim, int64_t tokens,
+                                 int64_t splits, uint16_t** masks, int64_t* mask_stride);
 
 /*
  * Allocation-free variant of popkv_sparse_attention (no counterpart in the

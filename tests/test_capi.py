@@ -60,7 +60,7 @@ def test_pack_rejects_bad_dtype_and_head_dim(lib):
 def test_select_rejects_budget_one(lib):
     dummy = ctypes.c_void_p(16)
     rc = lib.popkv_select(dummy, *_i64(4, 100, 100), None, ctypes.c_int64(0), ctypes.c_int64(1),
-                          dummy, None)
+                          dummy, None, ctypes.c_int64(0), ctypes.c_int64(0), None, None)
     assert rc == 1
 
 
@@ -68,7 +68,7 @@ def test_score_rejects_tokens_beyond_capacity(lib):
     dummy = ctypes.c_void_p(16)
     rc = lib.popkv_score(dummy, 2, *_i64(1, 32, 128), dummy, dummy, dummy, dummy,
                          *_i64(8, 64), 0, dummy, ctypes.c_int64(65), None, dummy,
-                         ctypes.c_int64(65), 0, None)
+                         ctypes.c_int64(65), None, 0, None)
     assert rc == 1
 
 

@@ -123,3 +123,27 @@ def test_attention_accepts_reference_int64_unsorted_indices():
     vs = torch.where(idx[..., None] == L, cv[0][h2k][:, None], vc[h2k[:, None], idx.clamp_max(L - 1)])
     ref = torch.nn.functional.scaled_dot_product_attention(q[0].float()[:, None], ks.float(), vs.float())[:, 0]
     torch.testing.assert_close(out[0].float().cpu(), ref, atol=2e-2, rtol=0)
+
+
+def test_premasked_attention_matches_index_path():
+    """select writing the workspace bitmask + premasked attention == indices + scatter path."""
+    g = torch.Generator().manual_seed(21)
+    B, KVH, QH, D, L, budget = 2, 4, 16, 128, 20000, 2048
+    kc = torch.randn(B, KVH, L + 1, D, generator=g).bfloat16().to(DEV)
+    vc = torch.randn(B, KVH, L + 1, D, generator=g).bfloat16().to(DEV)
+    q = torch.randn(B, QH, D, generator=g).bfloat16().to(DEV)
+    ck = torch.randn(B, KVH, D, generator=g).bfloat16().to(DEV)
+    cv = torch.randn(B, KVH, D, generator=g).bfloat16().to(DEV)
+    scores = torch.randn(B * QH, L, generator=g).to(DEV)
+    lens = torch.tensor([L, 9000], dtype=torch.int32, device=DEV)
+    ws = pk.new_workspace(B, QH, KVH, D, L, DEV)
+    for _ in range(2):  # the second round checks that the masks were cleared
+        idx = pk.select(scores, budget=budget, tokens=L, seq_len=lens, rows_per_seq=QH,
+                        attn_workspace=ws, attn_sizes=(B, QH, KVH, D, L, 0))
+        got = torch.empty_like(q)
+        pk.sparse_attention_premasked(q, kc, vc, tokens=L, current_keys=ck, current_values=cv,
+                                      seq_len=lens, workspace=ws, out=got)
+        ref = pk.sparse_attention(q, kc, vc, idx, budget=budget, tokens=L, current_keys=ck,
+                                  current_values=cv, seq_len=lens)
+        torch.testing.assert_close(got, ref, rtol=0, atol=0)
+        scores = scores.roll(1, dims=1)

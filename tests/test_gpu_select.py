@@ -77,3 +77,24 @@ def test_select_agrees_with_torch_topk_as_sets():
 def test_select_rejects_budget_one():
     with pytest.raises(ValueError):
         pk.select(torch.zeros(2, 10, device=DEV), budget=1)
+
+
+@pytest.mark.parametrize("G,L", [(4, 32768), (4, 3000), (16, 20000), (8, 131072)])
+def test_select_with_score_histogram_is_exact(G, L):
+    """score(hist=...) -> select(hist=...) equals select without the histogram, and the
+    histogram comes back zeroed (heads beyond 8 per KV head fall back inside select)."""
+    from conftest import synthetic_keys
+    KVH, D, budget = 2, 128, 4096
+    QH = KVH * G
+    k = synthetic_keys(KVH, L, D, seed=L, dtype=torch.bfloat16).to(DEV)
+    q = synthetic_keys(1, QH, D, seed=L + 1, dtype=torch.bfloat16).to(DEV)
+    h2k = (torch.arange(QH) // G).to(DEV)
+    packed = pk.pack_keys(k)
+    hist = pk.new_score_histogram(QH, DEV)
+    for _ in range(2):
+        scores = pk.score(q, packed, head_to_kv=h2k, tokens=L, hist=hist)
+        got = pk.select(scores.view(QH, L), budget=budget, hist=hist)
+        ref = pk.select(scores.view(QH, L), budget=budget)
+        torch.testing.assert_close(got, ref, rtol=0, atol=0)
+        assert int(hist.abs().sum()) == 0
+        np.testing.assert_array_equal(ref.cpu().numpy(), O.select(scores.view(QH, L).cpu().numpy(), budget=budget))
