@@ -241,19 +241,20 @@ def run_ours(args):
     sizes = (B, stack.q_heads, stack.kv_heads, D, tokens, 0)
 
     def run_stage(name, i):
-        if name == "score":
+        parts = name.split("+")
+        if "score" in parts:
             pk.score(stack.q_in[i], stack.packed[i], head_to_kv=stack.head_to_kv, tokens=tokens,
                      seq_len=stack.seq_len, out=stack.scores, hist=stack.score_hist)
-        elif name in ("select", "select+attention"):
+        if "select" in parts:
             pk.select(stack.scores.view(-1, stack.capacity), budget=budget, tokens=tokens,
                       seq_len=stack.seq_len, rows_per_seq=stack.q_heads, out=stack.indices[i],
                       attn_workspace=stack.workspace[i], attn_sizes=sizes, hist=stack.score_hist)
-            if name == "select+attention":  # the attention consumes (and clears) the masks
-                pk.sparse_attention_premasked(stack.q_in[i], stack.key_cache[i], stack.value_cache[i],
-                                              tokens=tokens, current_keys=stack.k_in[i],
-                                              current_values=stack.v_in[i], seq_len=stack.seq_len,
-                                              workspace=stack.workspace[i], out=stack.out[i])
-        elif name == "append":
+        if "attention" in parts:  # consumes (and clears) the masks select wrote
+            pk.sparse_attention_premasked(stack.q_in[i], stack.key_cache[i], stack.value_cache[i],
+                                          tokens=tokens, current_keys=stack.k_in[i],
+                                          current_values=stack.v_in[i], seq_len=stack.seq_len,
+                                          workspace=stack.workspace[i], out=stack.out[i])
+        if "append" in parts:
             pk.append_keys(stack.key_cache[i], stack.value_cache[i], stack.k_in[i], stack.v_in[i],
                            stack.packed[i], position=0, seq_len=stack.seq_len,
                            kv_heads_per_seq=stack.kv_heads)
@@ -269,9 +270,15 @@ def run_ours(args):
         stream.wait_stream(side)
         return g
 
-    for name in ("score", "select", "select+attention", "append"):
+    # Each select needs the histogram its score just built, and each attention the
+    # masks its select just wrote: time the prefixes of the layer pipeline and take
+    # differences.
+    timed = {}
+    for name in ("score+select+attention", "score", "score+select", "append"):
         for i in range(layers):
             run_stage(name, i)  # eager warm-up of this stage
+        if name == "score":
+            torch.cuda.synchronize()
         g = stage_graph(name)
         g.replay()
         torch.cuda.synchronize()
@@ -281,10 +288,18 @@ def run_ours(args):
             g.replay()
         b.record(stream)
         torch.cuda.synchronize()
-        stage_ms[name] = a.elapsed_time(b) / (reps * layers)
+        timed[name] = a.elapsed_time(b) / (reps * layers)
+        if name == "score":  # histograms accumulated without a select: start clean
+            stack.score_hist.zero_()
         del g
-    # Selection re-run by the select stage left its masks set: one attention pass clears them.
-    stage_ms["attention"] = stage_ms.pop("select+attention") - stage_ms["select"]
+    stage_ms["score"] = timed["score"]
+    stage_ms["select"] = timed["score+select"] - timed["score"]
+    stage_ms["attention"] = timed["score+select+attention"] - timed["score+select"]
+    stage_ms["append"] = timed["append"]
+    # The score+select replays left masks set: clear them with one attention pass.
+    for i in range(layers):
+        run_stage("attention", i)
+    torch.cuda.synchronize()
 
     # Union of selections per (sequence, KV head) -> attention's algorithmic bytes.
     L_now = stack.length

@@ -33,8 +33,20 @@ constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 16;
 constexpr int kSegMax = 2048;   // tokens per segment (multiple of 8)
 constexpr int kTileRows = 16;
-constexpr int kStages = 2;
+#ifndef POPKV_ATTN_STAGES
+#define POPKV_ATTN_STAGES 3
+#endif
+constexpr int kStages = POPKV_ATTN_STAGES;  // cp.async ring depth per warp
 constexpr int kMaxSplits = 1024;
+
+// Phase timestamps for tuning builds (-DPOPKV_ATTN_PROFILE): thread 0 of each CTA
+// records globaltimer at phase boundaries (8 slots per CTA).
+#ifdef POPKV_ATTN_PROFILE
+__device__ unsigned long long g_attn_marks[65536 * 8];
+#define ATTN_MARK(i) do { if (threadIdx.x == 0) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_attn_marks[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + (i)] = t; } } while (0)
+#else
+#define ATTN_MARK(i) do { } while (0)
+#endif
 
 struct AttnParams {
     const void* q;
@@ -74,6 +86,8 @@ __device__ __forceinline__ int64_t segment_len(int64_t L, int S) {
 
 // ------------------------------------------------------------- scatter kernel
 __global__ void scatter_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int row = blockIdx.y;  // b*QH + qh
     const int b = row / p.QH;
     const int qh = row - b * p.QH;
@@ -167,6 +181,8 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
 // costs a few L2 round trips.
 template <typename T>
 __global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float s_w[kMaxSplits];
     __shared__ float s_red[2][4];
     const int64_t row = blockIdx.x;  // b*QH + qh
@@ -271,7 +287,15 @@ template <> struct MmaOp<__half> {
 // Shared-memory plan of the tensor-core kernel (bytes).
 template <typename T, int D>
 struct MmaPlan {
-    static constexpr int LDS = D + 8;  // padded row: conflict-free ldmatrix
+    // Rows of 8 or 16 sixteen-byte chunks are stored unpadded with chunk c of row r
+    // at c ^ (r & 7) (conflict-free ldmatrix); other widths are padded by 16 bytes.
+    static constexpr int CPR = D * (int)sizeof(T) / 16;
+#ifdef POPKV_ATTN_NO_SWIZZLE
+    static constexpr bool SWZ = false;
+#else
+    static constexpr bool SWZ = CPR % 8 == 0;
+#endif
+    static constexpr int LDS = SWZ ? D : D + 8;
     static constexpr int kStageBytes = 2 * kTileRows * LDS * (int)sizeof(T);
     static constexpr int kRingBytes = kAttnWarps * kStages * kStageBytes;
     static constexpr int kMergeBytes = kAttnWarps * kMaxGroup * (D + 2) * 4;
@@ -281,6 +305,8 @@ struct MmaPlan {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     using Plan = MmaPlan<T, D>;
     constexpr int LDS = Plan::LDS;
     constexpr int NT8 = D / 8;   // output n-tiles
@@ -303,12 +329,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
     const int64_t seg = segment_len(L, p.S);
     const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
     const int64_t hi = imin64(lo + seg, L + 1);
-    const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
-                                    p.dense != 0);
-
+    ATTN_MARK(0);
     const T* q = static_cast<const T*>(p.q);
     const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
-    // Query fragments (A operand, heads g and g+8).
+    // Query fragments (A operand, heads g and g+8), loaded while the union is built.
     uint32_t qa[KS][4];
     {
         const uint32_t* q0 = reinterpret_cast<const uint32_t*>(q + (qrow0 + g) * D);
@@ -323,6 +347,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
             qa[kk][3] = h1 ? __ldg(q1 + c + 4) : 0u;
         }
     }
+    const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
+                                    p.dense != 0);
+    ATTN_MARK(1);
 
     const T* kc = static_cast<const T*>(p.kc);
     const T* vc = static_cast<const T*>(p.vc);
@@ -358,8 +385,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
                 ks += ch * EPC;
                 vs += ch * EPC;
             }
-            cp_async16(kd + r * LDS + ch * EPC, ks, bytes);
-            cp_async16(vd + r * LDS + ch * EPC, vs, bytes);
+            const int pch = Plan::SWZ ? (ch ^ (r & 7)) : ch;
+            cp_async16(kd + r * LDS + pch * EPC, ks, bytes);
+            cp_async16(vd + r * LDS + pch * EPC, vs, bytes);
         }
     };
 
@@ -394,7 +422,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
 #pragma unroll
             for (int k2 = 0; k2 < D / 32; ++k2) {
                 uint32_t bf[4];
-                ldmatrix_x4(bf, Ks + (nt * 8 + (lane & 7)) * LDS + k2 * 32 + (lane >> 3) * 8);
+                const int kch = k2 * 4 + (lane >> 3);
+                ldmatrix_x4(bf, Ks + (nt * 8 + (lane & 7)) * LDS +
+                                    (Plan::SWZ ? (kch ^ (lane & 7)) : kch) * 8);
                 MmaOp<T>::run(sc[nt], qa[2 * k2], bf[0], bf[1]);
                 MmaOp<T>::run(sc[nt], qa[2 * k2 + 1], bf[2], bf[3]);
             }
@@ -448,13 +478,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
 #pragma unroll
         for (int np = 0; np < D / 16; ++np) {
             uint32_t bf[4];
-            ldmatrix_x4_trans(bf, Vs + (((lane >> 3) & 1) * 8 + (lane & 7)) * LDS + np * 16 + (lane >> 4) * 8);
+            const int vch = np * 2 + (lane >> 4);
+            ldmatrix_x4_trans(bf, Vs + (((lane >> 3) & 1) * 8 + (lane & 7)) * LDS +
+                                      (Plan::SWZ ? (vch ^ (lane & 7)) : vch) * 8);
             MmaOp<T>::run(acc[2 * np], pa, bf[0], bf[1]);
             MmaOp<T>::run(acc[2 * np + 1], pa, bf[2], bf[3]);
         }
         __syncwarp();
     }
     cp_async_wait<0>();
+    ATTN_MARK(2);
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
         l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 1);
@@ -505,11 +538,14 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
         }
     }
     __syncthreads();
+    ATTN_MARK(3);
 }
 
 // SIMT variant (fp32 caches, or head_dim outside the tensor-core instances).
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads) attention_simt_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(128) unsigned char smem[];
     // [0, work_bytes): merge / combine scratch; then token list and masks.
     int* s_tok = reinterpret_cast<int*>(smem + p.work_bytes);
@@ -532,6 +568,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_simt_kernel(AttnParams
     const int64_t hi = imin64(lo + seg, L + 1);
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
                                     p.dense != 0);
+    ATTN_MARK(1);
     const T* q = static_cast<const T*>(p.q);
     const T* kc = static_cast<const T*>(p.kc);
     const T* vc = static_cast<const T*>(p.vc);
@@ -644,10 +681,10 @@ int launch_mma(const AttnParams& p, cudaStream_t st) {
     if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
     auto kern = attention_mma_kernel<T, D>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), kAttnThreads, smem, st>>>(p);
+    launch_pdl(kern, dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), dim3(kAttnThreads), smem, st, p);
     const int rc = check_launch("popkv_sparse_attention");
     if (rc != POPKV_OK) return rc;
-    combine_kernel<T><<<(unsigned)(p.B * p.QH), 128, 0, st>>>(p);
+    launch_pdl(combine_kernel<T>, dim3((unsigned)(p.B * p.QH)), dim3(128), 0, st, p);
     return check_launch("popkv_sparse_attention (combine)");
 }
 
@@ -659,10 +696,10 @@ int launch_simt(AttnParams p, cudaStream_t st) {
     if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
     auto kern = attention_simt_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), kAttnThreads, smem, st>>>(p);
+    launch_pdl(kern, dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), dim3(kAttnThreads), smem, st, p);
     const int rc = check_launch("popkv_sparse_attention");
     if (rc != POPKV_OK) return rc;
-    combine_kernel<T><<<(unsigned)(p.B * p.QH), 128, 0, st>>>(p);
+    launch_pdl(combine_kernel<T>, dim3((unsigned)(p.B * p.QH)), dim3(128), 0, st, p);
     return check_launch("popkv_sparse_attention (combine)");
 }
 
@@ -670,6 +707,12 @@ int launch_simt(AttnParams p, cudaStream_t st) {
 }  // namespace popkv
 
 using namespace popkv;
+
+#ifdef POPKV_ATTN_PROFILE
+extern "C" int attn_read_marks(unsigned long long* host, int n) {
+    return (int)cudaMemcpyFromSymbol(host, g_attn_marks, n * sizeof(unsigned long long));
+}
+#endif
 
 extern "C" size_t popkv_sparse_attention_workspace_bytes(int64_t batch, int64_t q_heads,
                                                          int64_t kv_heads, int64_t head_dim,
@@ -741,7 +784,7 @@ static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t
     if (mode == kFromIndices) {
         const int64_t per_row = (budget < tokens + 1 ? budget : tokens + 1);
         const dim3 grid((unsigned)((per_row + 255) / 256), (unsigned)(batch * q_heads));
-        scatter_kernel<<<grid, 256, 0, st>>>(p);
+        launch_pdl(scatter_kernel, grid, dim3(256), 0, st, p);
         const int rc = check_launch("popkv_sparse_attention (scatter)");
         if (rc != POPKV_OK) return rc;
     }

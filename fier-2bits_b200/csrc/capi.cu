@@ -30,6 +30,8 @@ int check_launch(const char* what) {
 
 namespace {
 __global__ void advance_kernel(int32_t* seq_len, int64_t batch, int32_t inc) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i < batch) seq_len[i] += inc;
 }
@@ -61,7 +63,7 @@ extern "C" int popkv_advance(int32_t* seq_len, int64_t batch, int32_t increment,
     if (batch < 0 || (batch > 0 && seq_len == nullptr))
         return fail(POPKV_ERR_INVALID_ARGUMENT, "seq_len must hold batch entries");
     if (batch == 0) return POPKV_OK;
-    advance_kernel<<<(unsigned)((batch + 255) / 256), 256, 0, as_stream(stream)>>>(seq_len, batch,
-                                                                                increment);
+    launch_pdl(advance_kernel, dim3((unsigned)((batch + 255) / 256)), dim3(256), 0, as_stream(stream),
+               seq_len, batch, increment);
     return check_launch("popkv_advance");
 }

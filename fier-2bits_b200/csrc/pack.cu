@@ -154,6 +154,8 @@ pack_kernel(const T* __restrict__ keys, int64_t tokens, int D, int64_t head_stri
             int64_t groups, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
             uint16_t* __restrict__ low, uint16_t* __restrict__ delta, int64_t capacity,
             int64_t token_offset, float* __restrict__ thresholds, bool vec_ok, bool ref_div) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const PackSmem s = carve<W>(smem_raw, D);
     const int64_t h = blockIdx.x / groups;
@@ -176,6 +178,8 @@ append_kernel(T* __restrict__ key_cache, T* __restrict__ value_cache, int64_t kv
               uint16_t* __restrict__ low, uint16_t* __restrict__ delta, int64_t capacity,
               const int32_t* __restrict__ seq_len, int64_t position, int64_t heads_per_seq,
               bool vec_ok, bool ref_div) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const PackSmem s = carve<W>(smem_raw, D);
     const int64_t h = blockIdx.x;
@@ -207,7 +211,8 @@ int launch_pack_t(const void* keys, int64_t heads, int64_t tokens, int D, int64_
     const size_t smem = pack_smem_bytes(D, W);
     auto kern = pack_kernel<T, W>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<dim3((unsigned)(heads * groups)), 32 * W, smem, st>>>(
+    launch_pdl(kern, dim3((unsigned)(heads * groups)), dim3(32 * W), smem, st,
+
         static_cast<const T*>(keys), tokens, D, stride, groups, sg, mg, lo, de, cap, off, thr,
         vec_ok, ref_div);
     return check_launch("popkv_pack");
@@ -221,7 +226,8 @@ int launch_append_t(void* kc, void* vc, int64_t heads, int64_t kv_cap, int D, co
     const size_t smem = pack_smem_bytes(D, W);
     auto kern = append_kernel<T, W>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<dim3((unsigned)heads), 32 * W, smem, st>>>(
+    launch_pdl(kern, dim3((unsigned)heads), dim3(32 * W), smem, st,
+
         static_cast<T*>(kc), static_cast<T*>(vc), kv_cap, D, static_cast<const T*>(nk),
         static_cast<const T*>(nv), sg, mg, lo, de, cap, seq_len, pos, hps, vec_ok, ref_div);
     return check_launch("popkv_append");

@@ -23,7 +23,7 @@ namespace popkv {
 namespace {
 
 constexpr int kScoreThreads = 256;
-constexpr int kTokensPerThread = 2;
+constexpr int kTokensPerThread = 4;
 constexpr int kTile = kScoreThreads * kTokensPerThread;
 constexpr int kBins = 2048;     // histogram of the top 11 bits of each score's order key
 constexpr int kHistHeads = 8;   // query heads per KV head covered by the in-CTA histogram
@@ -86,6 +86,8 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
              const int64_t* __restrict__ head_to_kv, int64_t tokens,
              const int32_t* __restrict__ seq_len, float* __restrict__ scores, int64_t stride,
              float scale, bool ref_div, uint32_t* __restrict__ score_hist, int hist_heads) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint32_t* s_hist = reinterpret_cast<uint32_t*>(smem_raw);         // [hist_heads][kBins]
     float* s_abs = reinterpret_cast<float*>(s_hist + hist_heads * kBins);  // [warps][W*32]
@@ -252,7 +254,8 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
     auto run = [&](auto kern) {
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, kScoreThreads, smem, st>>>(
+        launch_pdl(kern, grid, dim3(kScoreThreads), smem, st,
+
             static_cast<const TQ*>(q), (int)q_heads, D, sg, mg, lo, de, (int)kv_heads, cap,
             per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div, hist, hist_heads);
     };
@@ -286,8 +289,10 @@ extern "C" int popkv_score(const void* queries, int q_dtype, int64_t batch, int6
                            const uint16_t* low, const uint16_t* delta, int64_t kv_heads,
                            int64_t capacity, int cache_per_batch, const int64_t* head_to_kv,
                            int64_t tokens, const int32_t* seq_len, float* scores,
-                           int64_t score_stride, uint32_t* score_hist, int flags,
+                           int64_t score_stride, void* select_workspace, int flags,
                            popkv_stream_t stream) {
+    // The select workspace starts with the [rows][2048] uint32 histogram.
+    uint32_t* score_hist = static_cast<uint32_t*>(select_workspace);
     if (dtype_size(q_dtype) == 0)
         return fail(POPKV_ERR_UNSUPPORTED, "queries dtype %d is not fp32/fp16/bf16", q_dtype);
     if (batch < 0 || q_heads <= 0 || head_dim <= 0 || kv_heads <= 0)

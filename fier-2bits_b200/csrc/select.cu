@@ -5,41 +5,55 @@
 // scores' token indices in ascending index order, ties at the threshold broken
 // towards the lowest index, then L (the newest token), then -1 padding.
 //
-// B200 design: one 1024-thread CTA per row, exact in every case.
-//  1. Threshold guess.  With the scorer's histogram of the top 11 key bits, the
-//     bin holding the k-th largest score gives an exact lower bound T0.  Without
-//     it, rows longer than the candidate buffer draw 1024 evenly
-//     spaced scores, sort them in shared memory (bitonic) and take the sample
-//     whose rank corresponds to ~1.15 k of the row plus a margin: a lower bound
-//     T0 that almost surely leaves at least k scores at or above it.
-//  2. Candidates.  One pass over the row (16-byte loads, L2-resident scores)
-//     counts the scores >= T0 per warp with ballots, a second pass compacts them
-//     -- in index order -- into shared memory (about 1.3 k entries).
-//  3. Exact radix select (11/11/10-bit digits, warp-aggregated histograms with
-//     match.any) over the candidates only.
-//  4. Ranking with warp ballots over the index-ordered candidates writes the
-//     picks in ascending index order, plus -- optionally -- the per-KV-head token
-//     bitmask the fused attention consumes.
-// If the guess leaves fewer than k candidates, or more than the buffer holds
-// (heavy ties), steps 3-4 run over the whole row read from global memory instead:
-// slower, same result.  No CTA waits on another.
+// Two exact paths, both built on one idea: find a lower bound T0 for the k-th
+// largest score, compact the scores >= T0 (about 1.1-1.3 k of them) in index
+// order, run the exact radix select (11/11/10-bit digits, warp-aggregated
+// shared-memory histograms with match.any) over those candidates only, and rank
+// them with warp ballots so the picks come out in index order without a sort.
+//
+//  * With a select workspace (the decode pipeline): the scorer has already
+//    built each row's histogram of the top 11 key bits, which fixes the first
+//    radix digit exactly.  Kernel 1 (one 256-thread CTA per row and 4096-token
+//    chunk, i.e. the whole GPU) reads the histogram, derives T0 and compacts its
+//    chunk's candidates into the workspace; kernel 2 (one 1024-thread CTA per
+//    row) stitches the chunk lists, finishes digits 2-3, ranks and writes, and
+//    zeroes the histogram for the next step.
+//  * Without one: a single 1024-thread CTA per row sorts 1024 evenly spaced
+//    samples (bitonic, shared memory) to pick T0 at ~1.15 k plus a margin, then
+//    compacts and selects as above.
+// Either way, if the candidates turn out fewer than k or more than the shared
+// buffer holds (heavy ties), the radix select and ranking run over the whole row
+// instead: slower, same result.  Optionally the selection is also OR-ed into the
+// per-KV-head token bitmask the fused attention consumes.  No CTA waits on another.
 #include "common.cuh"
 
 namespace popkv {
 namespace {
 
-constexpr int kSelThreads = 1024;
-constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kBins = 2048;
-constexpr int kCandMax = 16384;  // candidates kept in shared memory (key + index: 128 KB)
+constexpr int kCandMax = 16384;   // candidates kept in shared memory (key + index: 128 KB)
 constexpr int kSample = 1024;
+constexpr int kChunk = 4096;      // tokens per candidate-compaction CTA
+constexpr int kChunkThreads = 256;
+constexpr int kMaxChunks = 1024;  // rows up to 4M tokens on the workspace path
+constexpr int kRowThreads = 1024;
+
+// Phase timestamps for tuning builds (-DPOPKV_SELECT_PROFILE): thread 0 of each row
+// records clock64() at the phase boundaries into a device array of 16 per row.
+#ifdef POPKV_SELECT_PROFILE
+__device__ long long g_select_marks[4096 * 16];
+#define SEL_MARK(i) do { if (threadIdx.x == 0) g_select_marks[blockIdx.x * 16 + (i)] = clock64(); } while (0)
+#else
+#define SEL_MARK(i) do { } while (0)
+#endif
 
 struct SelectShared {
     uint32_t hist[kBins];
-    uint32_t wsum[kSelWarps];
-    uint32_t wa[kSelWarps], wb[kSelWarps];
+    uint32_t wsum[32], wabove[32], wgt[32], weq[32];
+    uint32_t total;
     uint32_t sel_bin, sel_above;
     uint32_t count;
+    uint32_t chunk_off[kMaxChunks];
 };
 
 struct SelectArgs {
@@ -53,19 +67,45 @@ struct SelectArgs {
     uint16_t* masks;       // optional [rows / heads_per_kv][mask_stride] head bitmask
     int64_t mask_stride;
     int heads_per_kv;
-    uint32_t* hist;        // optional [rows][kBins] top-digit histogram from the scorer
     bool vec;
+    // select workspace (nullable)
+    uint32_t* hist;        // [rows][kBins]
+    uint32_t* counts;      // [rows][kMaxChunks]
+    uint32_t* ckey;        // [rows][tokens_pad]
+    int32_t* cidx;         // [rows][tokens_pad]
+    int64_t tokens_pad;
 };
 
-// Finds the bin of sh.hist where the count from the top first reaches `remaining`:
-// sh.sel_bin, sh.sel_above (count strictly above it) and sh.count (total).
-__device__ void find_bin(SelectShared& sh, uint32_t remaining) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int kPer = kBins / kSelThreads;
-    uint32_t local = 0u;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) local += sh.hist[tid * kPer + j];
-    uint32_t suffix = local;  // sum over lanes >= lane
+struct SelectWorkspace {
+    size_t hist, counts, ckey, cidx, total;
+    int64_t tokens_pad;
+};
+
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+SelectWorkspace select_layout(int64_t rows, int64_t tokens) {
+    SelectWorkspace w;
+    w.tokens_pad = (tokens + kChunk - 1) / kChunk * kChunk;
+    w.hist = 0;
+    w.counts = align256(sizeof(uint32_t) * rows * kBins);
+    w.ckey = w.counts + align256(sizeof(uint32_t) * rows * kMaxChunks);
+    w.cidx = w.ckey + align256(sizeof(uint32_t) * rows * w.tokens_pad);
+    w.total = w.cidx + align256(sizeof(int32_t) * rows * w.tokens_pad);
+    return w;
+}
+
+__device__ __forceinline__ int64_t row_length(const SelectArgs& a, int64_t row) {
+    int64_t L = a.seq_len ? static_cast<int64_t>(a.seq_len[row / a.rows_per_seq]) : a.tokens;
+    return L < a.tokens ? (L < 0 ? 0 : L) : a.tokens;
+}
+
+// Sum of `local` over the threads above this one (higher tid) and over all threads.
+template <int THREADS>
+__device__ __forceinline__ void block_suffix(uint32_t local, SelectShared& sh, uint32_t& above,
+                                             uint32_t& total) {
+    constexpr int NW = THREADS / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t suffix = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, o);
@@ -73,9 +113,63 @@ __device__ void find_bin(SelectShared& sh, uint32_t remaining) {
     }
     if (lane == 0) sh.wsum[warp] = suffix;
     __syncthreads();
-    uint32_t above = suffix - local;
-    for (int w = warp + 1; w < kSelWarps; ++w) above += sh.wsum[w];
-    if (tid == 0) sh.count = above + local;
+    if (warp == 0) {
+        const uint32_t v = lane < NW ? sh.wsum[lane] : 0u;
+        uint32_t x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_down_sync(0xffffffffu, x, o);
+            if (lane + o < 32) x += y;
+        }
+        sh.wabove[lane] = x - v;
+        if (lane == 0) sh.total = x;
+    }
+    __syncthreads();
+    above = suffix - local + sh.wabove[warp];
+    total = sh.total;
+}
+
+// Sum of `local` over the threads below this one, and over all threads.
+template <int THREADS>
+__device__ __forceinline__ void block_prefix(uint32_t local, SelectShared& sh, uint32_t& before,
+                                             uint32_t& total) {
+    constexpr int NW = THREADS / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) sh.wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t v = lane < NW ? sh.wsum[lane] : 0u;
+        uint32_t x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        sh.wabove[lane] = x - v;
+        if (lane == 31) sh.total = x;
+    }
+    __syncthreads();
+    before = incl - local + sh.wabove[warp];
+    total = sh.total;
+}
+
+// The bin of sh.hist where the count from the top first reaches `remaining`:
+// sh.sel_bin, sh.sel_above (count strictly above it) and sh.count (all bins).
+template <int THREADS>
+__device__ void find_bin(SelectShared& sh, uint32_t remaining) {
+    constexpr int kPer = kBins / THREADS;
+    const int tid = threadIdx.x;
+    uint32_t local = 0u;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) local += sh.hist[tid * kPer + j];
+    uint32_t above, total;
+    block_suffix<THREADS>(local, sh, above, total);
 #pragma unroll
     for (int j = kPer - 1; j >= 0; --j) {
         const uint32_t cnt = sh.hist[tid * kPer + j];
@@ -85,34 +179,41 @@ __device__ void find_bin(SelectShared& sh, uint32_t remaining) {
         }
         above += cnt;
     }
+    if (tid == 0) sh.count = total;
     __syncthreads();
 }
 
-// Exact k-th largest key among n keys given by `get` (3 radix passes); returns the
-// threshold key and how many keys equal to it are taken (the lowest-indexed ones).
-template <typename Get>
-__device__ void radix_threshold(Get get, int64_t n, uint32_t k, SelectShared& sh,
-                                uint32_t& thr, uint32_t& need) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    uint32_t prefix = 0u, pmask = 0u, remaining = k;
+// Exact k-th largest key among n keys given by `get`; returns the threshold key and
+// how many keys equal to it are taken (the lowest-indexed ones).  Passes before
+// `first_pass` are given by (prefix, pmask).
+template <int THREADS, typename Get>
+__device__ void radix_threshold(Get get, int64_t n, uint32_t k, SelectShared& sh, uint32_t& thr,
+                                uint32_t& need, int first_pass = 0, uint32_t prefix = 0u,
+                                uint32_t pmask = 0u) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    uint32_t remaining = k;
 #pragma unroll 1
-    for (int pass = 0; pass < 3; ++pass) {
+    for (int pass = first_pass; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
         const uint32_t dmask = pass == 2 ? 0x3ffu : 0x7ffu;
-        for (int i = tid; i < kBins; i += kSelThreads) sh.hist[i] = 0u;
+        for (int i = tid; i < kBins; i += THREADS) sh.hist[i] = 0u;
         __syncthreads();
-        for (int64_t i0 = 0; i0 < n; i0 += kSelThreads) {
+        for (int64_t i0 = 0; i0 < n; i0 += THREADS) {
             const int64_t i = i0 + tid;
             const bool active = i < n;
             const uint32_t key = active ? get(i) : 0u;
             const bool want = active && (key & pmask) == prefix;
-            if (!__any_sync(0xffffffffu, want)) continue;
             const uint32_t digit = (key >> shift) & dmask;
+            if (pass > 0) {  // within one top-digit bin the lower digits spread out
+                if (want) atomicAdd(&sh.hist[digit], 1u);
+                continue;
+            }
+            if (!__any_sync(0xffffffffu, want)) continue;
             const unsigned peers = __match_any_sync(0xffffffffu, want ? digit : 0xffffffffu);
             if (want && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[digit], __popc(peers));
         }
         __syncthreads();
-        find_bin(sh, remaining);
+        find_bin<THREADS>(sh, remaining);
         remaining -= sh.sel_above;
         prefix |= sh.sel_bin << shift;
         pmask |= dmask << shift;
@@ -124,11 +225,12 @@ __device__ void radix_threshold(Get get, int64_t n, uint32_t k, SelectShared& sh
 
 // Writes the picks (keys > thr, and the first `need` keys == thr) of n index-ordered
 // elements at their rank; idx(i) gives the token index of element i.
-template <typename Get, typename Idx>
+template <int THREADS, typename Get, typename Idx>
 __device__ void rank_and_write(Get get, Idx idx, int64_t n, uint32_t thr, uint32_t need,
                                SelectShared& sh, int32_t* out, uint32_t* mask_words, uint32_t bit) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t seg = ((n + kSelWarps - 1) / kSelWarps + 31) / 32 * 32;
+    constexpr int NW = THREADS / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t seg = ((n + NW - 1) / NW + 31) / 32 * 32;
     const int64_t w_lo = warp * seg;
     const int64_t w_hi = imin64(n, w_lo + seg);
     uint32_t gt = 0u, eq = 0u;
@@ -138,18 +240,21 @@ __device__ void rank_and_write(Get get, Idx idx, int64_t n, uint32_t thr, uint32
         gt += __popc(__ballot_sync(0xffffffffu, i < w_hi && key > thr));
         eq += __popc(__ballot_sync(0xffffffffu, i < w_hi && key == thr));
     }
-    if (lane == 0) { sh.wa[warp] = gt; sh.wb[warp] = eq; }
+    if (lane == 0) { sh.wgt[warp] = gt; sh.weq[warp] = eq; }
     __syncthreads();
-    if (tid == 0) {
-        uint32_t a = 0u, b = 0u;
-        for (int w = 0; w < kSelWarps; ++w) {
-            const uint32_t x = sh.wa[w], y = sh.wb[w];
-            sh.wa[w] = a; sh.wb[w] = b;
-            a += x; b += y;
+    if (warp == 0) {  // exclusive scan of the per-warp counts
+        uint32_t a = lane < NW ? sh.wgt[lane] : 0u, b = lane < NW ? sh.weq[lane] : 0u;
+        uint32_t ia = a, ib = b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t ya = __shfl_up_sync(0xffffffffu, ia, o);
+            const uint32_t yb = __shfl_up_sync(0xffffffffu, ib, o);
+            if (lane >= o) { ia += ya; ib += yb; }
         }
+        if (lane < NW) { sh.wgt[lane] = ia - a; sh.weq[lane] = ib - b; }
     }
     __syncthreads();
-    uint32_t gt_run = sh.wa[warp], eq_run = sh.wb[warp];
+    uint32_t gt_run = sh.wgt[warp], eq_run = sh.weq[warp];
     const unsigned lt_mask = (1u << lane) - 1u;
     for (int64_t e = w_lo; e < w_hi; e += 32) {
         const int64_t i = e + lane;
@@ -160,8 +265,7 @@ __device__ void rank_and_write(Get get, Idx idx, int64_t n, uint32_t thr, uint32
         const unsigned be = __ballot_sync(0xffffffffu, is_eq);
         const uint32_t g_before = gt_run + __popc(bg & lt_mask);
         const uint32_t e_before = eq_run + __popc(be & lt_mask);
-        const bool take = is_gt || (is_eq && e_before < need);
-        if (take) {
+        if (is_gt || (is_eq && e_before < need)) {
             const int32_t t = idx(i);
             out[g_before + min(e_before, need)] = t;
             if (mask_words) atomicOr(mask_words + (t >> 1), bit << ((t & 1) * 16));
@@ -171,61 +275,78 @@ __device__ void rank_and_write(Get get, Idx idx, int64_t n, uint32_t thr, uint32
     }
 }
 
-__global__ void __launch_bounds__(kSelThreads, 1) select_kernel(SelectArgs a) {
+struct RowOut {
+    int32_t* out;
+    uint32_t* mask_words;
+    uint32_t bit;
+};
+
+__device__ __forceinline__ RowOut row_output(const SelectArgs& a, int64_t row) {
+    RowOut r;
+    r.out = a.indices + row * a.budget;
+    r.mask_words = nullptr;
+    r.bit = 0u;
+    if (a.masks != nullptr) {
+        const int64_t b = row / a.rows_per_seq;
+        const int64_t qh = row - b * a.rows_per_seq;
+        const int64_t kv_per_seq = a.rows_per_seq / a.heads_per_kv;
+        r.mask_words = reinterpret_cast<uint32_t*>(
+            a.masks + (b * kv_per_seq + qh / a.heads_per_kv) * a.mask_stride);
+        r.bit = 1u << (qh % a.heads_per_kv);
+    }
+    return r;
+}
+
+// Newest token, padding and the all/nothing cases; returns true when the row is done.
+__device__ bool write_trivial(const SelectArgs& a, const RowOut& r, int64_t L, int64_t k,
+                              int threads) {
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        r.out[k] = static_cast<int32_t>(L);
+        if (r.mask_words) atomicOr(r.mask_words + (L >> 1), r.bit << ((L & 1) * 16));
+    }
+    for (int64_t j = k + 1 + tid; j < a.budget; j += threads) r.out[j] = -1;
+    if (k == 0) return true;
+    if (k == L) {
+        for (int64_t i = tid; i < L; i += threads) {
+            r.out[i] = static_cast<int32_t>(i);
+            if (r.mask_words) atomicOr(r.mask_words + (i >> 1), r.bit << ((i & 1) * 16));
+        }
+        return true;
+    }
+    return false;
+}
+
+// Exact selection of the whole row read from global memory (the fallback).
+__device__ void select_whole_row(const float* src, int64_t L, int64_t k, SelectShared& sh,
+                                 const RowOut& r) {
+    uint32_t thr, need;
+    auto get = [&](int64_t i) { return order_key(__ldg(src + i)); };
+    auto idx = [&](int64_t i) { return static_cast<int32_t>(i); };
+    radix_threshold<kRowThreads>(get, L, static_cast<uint32_t>(k), sh, thr, need);
+    rank_and_write<kRowThreads>(get, idx, L, thr, need, sh, r.out, r.mask_words, r.bit);
+}
+
+// ---------------------------------------------------------------- one kernel
+__global__ void __launch_bounds__(kRowThreads, 1) select_kernel(SelectArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) uint32_t s_dyn[];
     uint32_t* cand_key = s_dyn;                                          // [kCandMax]
     int32_t* cand_idx = reinterpret_cast<int32_t*>(s_dyn + kCandMax);     // [kCandMax]
     __shared__ SelectShared sh;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t row = blockIdx.x;
-    int64_t L = a.seq_len ? static_cast<int64_t>(a.seq_len[row / a.rows_per_seq]) : a.tokens;
-    L = L < a.tokens ? (L < 0 ? 0 : L) : a.tokens;
+    const int64_t L = row_length(a, row);
     const int64_t k = a.budget - 1 < L ? a.budget - 1 : L;
-    int32_t* out = a.indices + row * a.budget;
     const float* src = a.scores + row * a.stride;
-    uint32_t* mask_words = nullptr;
-    uint32_t bit = 0u;
-    if (a.masks != nullptr) {
-        const int64_t b = row / a.rows_per_seq;
-        const int64_t qh = row - b * a.rows_per_seq;
-        const int64_t kv_per_seq = a.rows_per_seq / a.heads_per_kv;
-        mask_words = reinterpret_cast<uint32_t*>(
-            a.masks + (b * kv_per_seq + qh / a.heads_per_kv) * a.mask_stride);
-        bit = 1u << (qh % a.heads_per_kv);
-    }
-    bool hist_ok = false;
-    if (a.hist != nullptr) {  // the scorer's top-digit histogram of this row (zeroed for next use)
-        uint32_t* hrow = a.hist + row * kBins;
-        for (int i = tid; i < kBins; i += kSelThreads) {
-            sh.hist[i] = hrow[i];
-            hrow[i] = 0u;
-        }
-        __syncthreads();
-        if (k > 0 && k < L) {
-            find_bin(sh, static_cast<uint32_t>(k));
-            hist_ok = sh.count == static_cast<uint32_t>(L);
-        }
-    }
-    if (tid == 0) {
-        out[k] = static_cast<int32_t>(L);
-        if (mask_words) atomicOr(mask_words + (L >> 1), bit << ((L & 1) * 16));
-    }
-    for (int64_t j = k + 1 + tid; j < a.budget; j += kSelThreads) out[j] = -1;
-    if (k == 0) return;
-    if (k == L) {
-        for (int64_t i = tid; i < L; i += kSelThreads) {
-            out[i] = static_cast<int32_t>(i);
-            if (mask_words) atomicOr(mask_words + (i >> 1), bit << ((i & 1) * 16));
-        }
-        return;
-    }
+    const RowOut r = row_output(a, row);
+    SEL_MARK(0);
+    if (write_trivial(a, r, L, k, kRowThreads)) return;
 
     // 1. Lower-bound threshold from a sorted sample (rows that do not fit whole).
     uint32_t t0 = 0u;
-    if (hist_ok) {
-        t0 = sh.sel_bin << 21;  // lowest key of the bin holding the k-th largest score
-        __syncthreads();
-    } else if (L > kCandMax) {
+    if (L > kCandMax) {
         uint32_t* s = cand_key;
         s[tid] = order_key(__ldg(src + (static_cast<int64_t>(tid) * L) / kSample));
         for (int size = 2; size <= kSample; size <<= 1) {
@@ -239,14 +360,15 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_kernel(SelectArgs a) {
             }
         }
         __syncthreads();
-        int64_t r = (kSample * k * 115) / (L * 100) + 25;  // rank ~1.15 k/L of the sample + margin
-        if (r > kSample) r = kSample;
-        t0 = s[r - 1];
+        int64_t rk = (kSample * k * 115) / (L * 100) + 25;  // rank ~1.15 k/L of the sample + margin
+        if (rk > kSample) rk = kSample;
+        t0 = s[rk - 1];
         __syncthreads();
     }
+    SEL_MARK(1);
 
     // 2. Count and compact the scores >= t0 in index order (warp-contiguous segments).
-    const int64_t seg = ((L + kSelWarps - 1) / kSelWarps + 127) / 128 * 128;
+    const int64_t seg = ((L + 31) / 32 + 127) / 128 * 128;
     const int64_t w_lo = imin64(warp * seg, L);
     const int64_t w_hi = imin64(w_lo + seg, L);
     auto flags4 = [&](int64_t i4, uint32_t (&key)[4]) -> uint32_t {
@@ -271,52 +393,191 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_kernel(SelectArgs a) {
         uint32_t key[4];
         wc += __reduce_add_sync(0xffffffffu, __popc(flags4(e + 4 * lane, key)));
     }
-    if (lane == 0) sh.wa[warp] = wc;
-    __syncthreads();
-    if (tid == 0) {
-        uint32_t acc = 0u;
-        for (int w = 0; w < kSelWarps; ++w) { const uint32_t x = sh.wa[w]; sh.wa[w] = acc; acc += x; }
-        sh.count = acc;
+    uint32_t wbase, nc;
+    block_prefix<kRowThreads>(lane == 0 ? wc : 0u, sh, wbase, nc);
+    wbase = __shfl_sync(0xffffffffu, wbase, 0);
+    SEL_MARK(2);
+    if (nc < static_cast<uint32_t>(k) || nc > static_cast<uint32_t>(kCandMax)) {
+        select_whole_row(src, L, k, sh, r);
+        return;
+    }
+    uint32_t base = wbase;
+    for (int64_t e = w_lo; e < w_hi; e += 128) {
+        uint32_t key[4];
+        const uint32_t f = flags4(e + 4 * lane, key);
+        const uint32_t c = __popc(f);
+        uint32_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        uint32_t pos = base + incl - c;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if ((f >> j) & 1u) {
+                cand_key[pos] = key[j];
+                cand_idx[pos] = static_cast<int32_t>(e + 4 * lane + j);
+                ++pos;
+            }
+        }
+        base += __shfl_sync(0xffffffffu, incl, 31);
     }
     __syncthreads();
-    const uint32_t nc = sh.count;
-    const bool fallback = nc < static_cast<uint32_t>(k) || nc > static_cast<uint32_t>(kCandMax);
-    if (!fallback) {
-        uint32_t base = sh.wa[warp];
-        for (int64_t e = w_lo; e < w_hi; e += 128) {
-            uint32_t key[4];
-            const uint32_t f = flags4(e + 4 * lane, key);
-            const uint32_t c = __popc(f);
-            uint32_t incl = c;
+    SEL_MARK(3);
+    uint32_t thr, need;
+    auto get = [&](int64_t i) { return cand_key[i]; };
+    auto idx = [&](int64_t i) { return cand_idx[i]; };
+    radix_threshold<kRowThreads>(get, nc, static_cast<uint32_t>(k), sh, thr, need);
+    SEL_MARK(4);
+    rank_and_write<kRowThreads>(get, idx, nc, thr, need, sh, r.out, r.mask_words, r.bit);
+    SEL_MARK(5);
+}
+
+// ------------------------------------------------- workspace path: kernel 1
+// One CTA per (row, 4096-token chunk): threshold bin from the scorer's histogram,
+// then the chunk's scores >= T0 compacted in index order into the workspace.
+__global__ void __launch_bounds__(kChunkThreads) select_candidates_kernel(SelectArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ SelectShared sh;
+    const int tid = threadIdx.x;
+    const int64_t row = blockIdx.y;
+    const int64_t c = blockIdx.x;
+    const int64_t L = row_length(a, row);
+    const int64_t k = a.budget - 1 < L ? a.budget - 1 : L;
+    const int64_t lo = c * kChunk;
+    uint32_t* count_out = a.counts + row * kMaxChunks + c;
+    if (k == 0 || k == L || lo >= L) {
+        if (tid == 0) *count_out = 0u;
+        return;
+    }
+    const int64_t hi = imin64(lo + kChunk, L);
+    const float* src = a.scores + row * a.stride;
+    constexpr int PER = kChunk / kChunkThreads;  // 16 consecutive scores per thread
+    const int64_t first = lo + static_cast<int64_t>(tid) * PER;
+    uint32_t key[PER];
+    bool in[PER];
+    if (a.vec && first + PER <= hi) {  // score loads first: they do not need the threshold
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            uint32_t pos = base + incl - c;
+        for (int q = 0; q < PER / 4; ++q) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + first) + q);
+            key[4 * q] = order_key(v.x); key[4 * q + 1] = order_key(v.y);
+            key[4 * q + 2] = order_key(v.z); key[4 * q + 3] = order_key(v.w);
+        }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if ((f >> j) & 1u) {
-                    cand_key[pos] = key[j];
-                    cand_idx[pos] = static_cast<int32_t>(e + 4 * lane + j);
-                    ++pos;
+        for (int j = 0; j < PER; ++j) in[j] = true;
+    } else {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            in[j] = first + j < hi;
+            key[j] = in[j] ? order_key(__ldcg(src + first + j)) : 0u;
+        }
+    }
+    const uint32_t* hrow = a.hist + row * kBins;
+    for (int i = tid; i < kBins; i += kChunkThreads) sh.hist[i] = __ldcg(hrow + i);
+    __syncthreads();
+    find_bin<kChunkThreads>(sh, static_cast<uint32_t>(k));
+    // A histogram that does not add up to L (heads the scorer skipped) makes every
+    // score a candidate; the finishing kernel then works from the whole row.
+    const uint32_t t0 = sh.count == static_cast<uint32_t>(L) ? (sh.sel_bin << 21) : 0u;
+    uint32_t f = 0u;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) f |= static_cast<uint32_t>(in[j] && key[j] >= t0) << j;
+    uint32_t before, total;
+    block_prefix<kChunkThreads>(__popc(f), sh, before, total);
+    uint32_t* ck = a.ckey + row * a.tokens_pad + lo;
+    int32_t* ci = a.cidx + row * a.tokens_pad + lo;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        if ((f >> j) & 1u) {
+            ck[before] = key[j];
+            ci[before] = static_cast<int32_t>(first + j);
+            ++before;
+        }
+    }
+    if (tid == 0) *count_out = total;
+}
+
+// ------------------------------------------------- workspace path: kernel 2
+__global__ void __launch_bounds__(kRowThreads, 1) select_finish_kernel(SelectArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) uint32_t s_dyn[];
+    uint32_t* cand_key = s_dyn;
+    int32_t* cand_idx = reinterpret_cast<int32_t*>(s_dyn + kCandMax);
+    __shared__ SelectShared sh;
+    const int tid = threadIdx.x;
+    const int64_t row = blockIdx.x;
+    const int64_t L = row_length(a, row);
+    const int64_t k = a.budget - 1 < L ? a.budget - 1 : L;
+    const float* src = a.scores + row * a.stride;
+    const RowOut r = row_output(a, row);
+    uint32_t* hrow = a.hist + row * kBins;
+    SEL_MARK(0);
+    const int64_t nchunks = (L + kChunk - 1) / kChunk;
+    const uint32_t cnt = tid < nchunks ? __ldcg(a.counts + row * kMaxChunks + tid) : 0u;
+    for (int i = tid; i < kBins; i += kRowThreads) {  // read, and zero for the next step
+        sh.hist[i] = __ldcg(hrow + i);
+        hrow[i] = 0u;
+    }
+    __syncthreads();
+    if (write_trivial(a, r, L, k, kRowThreads)) return;
+    find_bin<kRowThreads>(sh, static_cast<uint32_t>(k));
+    const bool hist_ok = sh.count == static_cast<uint32_t>(L);
+    const uint32_t bin = sh.sel_bin, above = sh.sel_above;
+    uint32_t off, nc;
+    block_prefix<kRowThreads>(cnt, sh, off, nc);
+    if (tid < nchunks) sh.chunk_off[tid] = off;
+    __syncthreads();
+    SEL_MARK(1);
+    if (nc < static_cast<uint32_t>(k) || nc > static_cast<uint32_t>(kCandMax)) {
+        select_whole_row(src, L, k, sh, r);
+        return;
+    }
+    // Stitch the chunk lists: every candidate position finds its chunk by binary
+    // search, so all loads are independent.
+    {
+        constexpr int kUnroll = 4;
+        const uint32_t* ck = a.ckey + row * a.tokens_pad;
+        const int32_t* ci = a.cidx + row * a.tokens_pad;
+        for (uint32_t p0 = 0; p0 < nc; p0 += kRowThreads * kUnroll) {
+            uint32_t kv[kUnroll];
+            int32_t iv[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const uint32_t p = p0 + u * kRowThreads + tid;
+                if (p < nc) {
+                    int lo = 0, hi = static_cast<int>(nchunks) - 1;  // last chunk with offset <= p
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (sh.chunk_off[mid] <= p) lo = mid; else hi = mid - 1;
+                    }
+                    const int64_t src = static_cast<int64_t>(lo) * kChunk + (p - sh.chunk_off[lo]);
+                    kv[u] = __ldcg(ck + src);
+                    iv[u] = __ldcg(ci + src);
                 }
             }
-            base += __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const uint32_t p = p0 + u * kRowThreads + tid;
+                if (p < nc) { cand_key[p] = kv[u]; cand_idx[p] = iv[u]; }
+            }
         }
-        __syncthreads();
-        uint32_t thr, need;
-        auto get = [&](int64_t i) { return cand_key[i]; };
-        auto idx = [&](int64_t i) { return cand_idx[i]; };
-        radix_threshold(get, nc, static_cast<uint32_t>(k), sh, thr, need);
-        rank_and_write(get, idx, nc, thr, need, sh, out, mask_words, bit);
-    } else {
-        uint32_t thr, need;
-        auto get = [&](int64_t i) { return order_key(__ldg(src + i)); };
-        auto idx = [&](int64_t i) { return static_cast<int32_t>(i); };
-        radix_threshold(get, L, static_cast<uint32_t>(k), sh, thr, need);
-        rank_and_write(get, idx, L, thr, need, sh, out, mask_words, bit);
     }
+    __syncthreads();
+    SEL_MARK(2);
+    uint32_t thr, need;
+    auto get = [&](int64_t i) { return cand_key[i]; };
+    auto idx = [&](int64_t i) { return cand_idx[i]; };
+    if (hist_ok)  // the histogram fixed the top digit: start at the second pass
+        radix_threshold<kRowThreads>(get, nc, static_cast<uint32_t>(k) - above, sh, thr, need, 1,
+                                     bin << 21, 0x7ffu << 21);
+    else
+        radix_threshold<kRowThreads>(get, nc, static_cast<uint32_t>(k), sh, thr, need);
+    SEL_MARK(3);
+    rank_and_write<kRowThreads>(get, idx, nc, thr, need, sh, r.out, r.mask_words, r.bit);
+    SEL_MARK(4);
 }
 
 }  // namespace
@@ -324,11 +585,22 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_kernel(SelectArgs a) {
 
 using namespace popkv;
 
+#ifdef POPKV_SELECT_PROFILE
+extern "C" int sel_read_marks(long long* host, int n) {
+    return (int)cudaMemcpyFromSymbol(host, g_select_marks, n * sizeof(long long));
+}
+#endif
+
+extern "C" size_t popkv_select_workspace_bytes(int64_t rows, int64_t tokens) {
+    if (rows <= 0 || tokens < 0) return 0;
+    return select_layout(rows, tokens).total;
+}
+
 extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_stride,
                             int64_t tokens, const int32_t* seq_len, int64_t rows_per_seq,
                             int64_t budget, int32_t* indices, uint16_t* head_masks,
-                            int64_t mask_stride, int64_t heads_per_kv, uint32_t* score_hist,
-                            popkv_stream_t stream) {
+                            int64_t mask_stride, int64_t heads_per_kv, void* select_workspace,
+                            size_t select_workspace_bytes, popkv_stream_t stream) {
     if (rows < 0 || tokens < 0 || score_stride < tokens)
         return fail(POPKV_ERR_INVALID_ARGUMENT, "invalid select shape (rows %lld, tokens %lld, stride %lld)",
                     (long long)rows, (long long)tokens, (long long)score_stride);
@@ -346,15 +618,38 @@ extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_str
     }
     if (rows == 0) return POPKV_OK;
     if (!indices || (tokens > 0 && !scores)) return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
-    SelectArgs a;
+    SelectArgs a = {};
     a.scores = scores; a.stride = score_stride; a.tokens = tokens; a.seq_len = seq_len;
     a.rows_per_seq = rows_per_seq > 0 ? rows_per_seq : rows;
     a.budget = budget; a.indices = indices; a.masks = head_masks; a.mask_stride = mask_stride;
     a.heads_per_kv = (int)(heads_per_kv > 0 ? heads_per_kv : 1);
-    a.hist = score_hist;
     a.vec = aligned(scores, 16) && score_stride % 4 == 0;
     const size_t smem = (size_t)kCandMax * 8;
+    const cudaStream_t st = as_stream(stream);
+    if (select_workspace != nullptr) {
+        const SelectWorkspace w = select_layout(rows, tokens);
+        if (select_workspace_bytes < w.total)
+            return fail(POPKV_ERR_WORKSPACE, "select workspace of %zu bytes, %zu needed",
+                        select_workspace_bytes, w.total);
+        if (!aligned(select_workspace, 256)) return fail(POPKV_ERR_ALIGNMENT, "select workspace needs 256-byte alignment");
+        if (tokens > (int64_t)kMaxChunks * kChunk) return fail(POPKV_ERR_UNSUPPORTED, "row too long for the select workspace");
+        unsigned char* base = static_cast<unsigned char*>(select_workspace);
+        a.hist = reinterpret_cast<uint32_t*>(base + w.hist);
+        a.counts = reinterpret_cast<uint32_t*>(base + w.counts);
+        a.ckey = reinterpret_cast<uint32_t*>(base + w.ckey);
+        a.cidx = reinterpret_cast<int32_t*>(base + w.cidx);
+        a.tokens_pad = w.tokens_pad;
+        const int64_t chunks = (tokens + kChunk - 1) / kChunk;
+        if (chunks > 0) {
+            launch_pdl(select_candidates_kernel, dim3((unsigned)chunks, (unsigned)rows), dim3(kChunkThreads), 0, st, a);
+            const int rc = check_launch("popkv_select (candidates)");
+            if (rc != POPKV_OK) return rc;
+        }
+        cudaFuncSetAttribute(select_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        launch_pdl(select_finish_kernel, dim3((unsigned)rows), dim3(kRowThreads), smem, st, a);
+        return check_launch("popkv_select");
+    }
     cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    select_kernel<<<(unsigned)rows, kSelThreads, smem, as_stream(stream)>>>(a);
+    launch_pdl(select_kernel, dim3((unsigned)rows), dim3(kRowThreads), smem, st, a);
     return check_launch("popkv_select");
 }

@@ -53,11 +53,12 @@ void check_packed(const std::vector<at::Tensor>& packed) {
                 "packed tensors are [KVH, capacity, words] or [B, KVH, capacity, words]");
 }
 
-uint32_t* hist_ptr(const c10::optional<at::Tensor>& hist, int64_t rows) {
-    if (!hist) return nullptr;
-    CHECK_CUDA(*hist); CHECK_CONTIGUOUS(*hist); CHECK_DTYPE(*hist, at::kInt);
-    TORCH_CHECK(hist->numel() == rows * 2048, "score histogram must be int32 [rows, 2048]");
-    return reinterpret_cast<uint32_t*>(hist->data_ptr<int32_t>());
+void* select_ws_ptr(const c10::optional<at::Tensor>& ws, int64_t rows, int64_t tokens) {
+    if (!ws) return nullptr;
+    CHECK_CUDA(*ws); CHECK_CONTIGUOUS(*ws);
+    TORCH_CHECK((size_t)ws->nbytes() >= popkv_select_workspace_bytes(rows, tokens),
+                "select workspace too small for ", rows, " rows of ", tokens, " tokens");
+    return ws->data_ptr();
 }
 
 std::vector<at::Tensor> pack(const at::Tensor& keys, int64_t token_capacity, int64_t flags,
@@ -181,7 +182,7 @@ at::Tensor score(const at::Tensor& queries, const at::Tensor& k_sign, const at::
                                reinterpret_cast<const uint16_t*>(delta.data_ptr<at::Half>()),
                                kv_heads, cap, per_batch ? 1 : 0, head_to_kv.data_ptr<int64_t>(),
                                tokens, sl, scores.data_ptr<float>(), scores.size(2),
-                               hist_ptr(hist, batch * q_heads), (int)flags, stream_of(queries));
+                               select_ws_ptr(hist, batch * q_heads, tokens), (int)flags, stream_of(queries));
     check_status(rc, "popkv_score");
     return scores;
 }
@@ -226,7 +227,8 @@ at::Tensor select_topk(const at::Tensor& scores, int64_t budget, int64_t tokens,
     }
     const int rc = popkv_select(scores.data_ptr<float>(), rows, stride, tokens, sl, rows_per_seq,
                                 budget, idx.data_ptr<int32_t>(), masks, mask_stride, heads_per_kv,
-                                hist_ptr(hist, rows), stream_of(scores));
+                                select_ws_ptr(hist, rows, tokens), hist ? (size_t)hist->nbytes() : 0,
+                                stream_of(scores));
     check_status(rc, "popkv_select");
     return idx;
 }
@@ -382,6 +384,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("seq_len") = py::none(), py::arg("workspace") = py::none(),
           py::arg("splits") = 0, py::arg("out") = py::none());
     m.def("workspace_bytes", &workspace_bytes);
+    m.def("select_workspace_bytes", [](int64_t rows, int64_t tokens) {
+        return (int64_t)popkv_select_workspace_bytes(rows, tokens);
+    });
     m.def("advance", &advance);
     m.def("version", &popkv_version);
 }

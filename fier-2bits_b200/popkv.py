@@ -202,7 +202,7 @@ class RetrievalStack:
                        for _ in range(layers)]
         self.head_to_kv = (torch.arange(QH, device=dev) // (QH // H)).to(torch.int64)
         self.scores = torch.empty(B, QH, self.capacity, dtype=torch.float32, device=dev)
-        self.score_hist = pk.new_score_histogram(B * QH, dev)
+        self.score_hist = pk.new_select_workspace(B * QH, self.max_tokens, dev)
         self.indices = [torch.empty(B * QH, budget, dtype=torch.int32, device=dev) for _ in range(layers)]
         self.workspace = [pk.new_workspace(B, QH, H, head_dim, self.max_tokens, dev) for _ in range(layers)]
         self.seq_len = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -215,6 +215,9 @@ class RetrievalStack:
         self.gathered = (torch.zeros(layers, self.world * B, QH, head_dim, dtype=dtype, device=dev)
                          if self.world > 1 else None)
         self.graph = None
+        # The append of a layer only has to follow that layer's score, so it runs on a
+        # side stream in parallel with select and attention; steps join it at the end.
+        self.side = torch.cuda.Stream(device=dev)
 
     # ------------------------------------------------------------------ setup
     def prefill(self, layer: int, keys: torch.Tensor, values: torch.Tensor) -> None:
@@ -237,6 +240,11 @@ class RetrievalStack:
         tokens = self.max_tokens
         pk.score(self.q_in[i], self.packed[i], head_to_kv=self.head_to_kv, tokens=tokens,
                  seq_len=self.seq_len, out=self.scores, hist=self.score_hist)
+        self.side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.side):
+            pk.append_keys(self.key_cache[i], self.value_cache[i], self.k_in[i], self.v_in[i],
+                           self.packed[i], position=0, seq_len=self.seq_len,
+                           kv_heads_per_seq=self.kv_heads)
         sizes = (self.batch, self.q_heads, self.kv_heads, self.head_dim, tokens, 0)
         pk.select(self.scores.view(-1, self.capacity), budget=self.budget, tokens=tokens,
                   seq_len=self.seq_len, rows_per_seq=self.q_heads, out=self.indices[i],
@@ -245,9 +253,6 @@ class RetrievalStack:
                                       tokens=tokens, current_keys=self.k_in[i],
                                       current_values=self.v_in[i], seq_len=self.seq_len,
                                       workspace=self.workspace[i], out=self.out[i])
-        pk.append_keys(self.key_cache[i], self.value_cache[i], self.k_in[i], self.v_in[i],
-                       self.packed[i], position=0, seq_len=self.seq_len,
-                       kv_heads_per_seq=self.kv_heads)
         if self.world > 1:
             import torch.distributed as dist
             dist.all_gather_into_tensor(self.gathered[i], self.out[i], group=self.group)
@@ -255,6 +260,7 @@ class RetrievalStack:
     def _step_launches(self) -> None:
         for i in range(self.layers):
             self._layer(i)
+        torch.cuda.current_stream().wait_stream(self.side)
         pk.advance(self.seq_len, 1)
 
     def step(self, q=None, k=None, v=None) -> torch.Tensor:

@@ -62,8 +62,8 @@ def score(queries: torch.Tensor, packed, *, head_to_kv: torch.Tensor, tokens: in
 
     queries [B, QH, D]; packed [KVH, cap, W] (shared by the batch, as in the
     reference) or [B, KVH, cap, W] (one cache per sequence) -> fp32 [B, QH, tokens].
-    ``hist`` (int32 [B*QH, 2048], zero) collects each row's top-11-bit key histogram
-    for ``select(hist=...)``, which consumes and re-zeroes it.
+    ``hist`` (a select workspace from ``new_select_workspace(B*QH, tokens)``) collects
+    each row's top-11-bit key histogram for ``select(hist=...)``, which consumes it.
     """
     if queries.ndim != 3 or not queries.is_cuda or not queries.is_contiguous():
         raise ValueError("queries must be contiguous CUDA [batch, query heads, head dim]")
@@ -142,9 +142,10 @@ def sparse_attention(queries: torch.Tensor, key_cache: torch.Tensor, value_cache
                                         workspace, int(splits), out)
 
 
-def new_score_histogram(rows: int, device) -> torch.Tensor:
-    """Zeroed int32 [rows, 2048] histogram shared by ``score`` and ``select``."""
-    return torch.zeros(rows, 2048, dtype=torch.int32, device=device)
+def new_select_workspace(rows: int, tokens: int, device) -> torch.Tensor:
+    """Zero-filled select workspace shared by ``score(hist=)`` and ``select(hist=)``."""
+    n = int(extension().select_workspace_bytes(int(rows), int(tokens)))
+    return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
 def workspace_bytes(batch: int, q_heads: int, kv_heads: int, head_dim: int, tokens: int,

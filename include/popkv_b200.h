@@ -104,17 +104,18 @@ int popkv_append(void* key_cache, void* value_cache, int dtype, int64_t heads,
  * queries: [batch, q_heads, head_dim] of q_dtype; head_to_kv: int64 [q_heads] (device).
  * scores: fp32 [batch, q_heads, score_stride]; tokens 0..L-1 of every row are written.
  * Requires tokens <= capacity and tokens <= score_stride.
- * score_hist (nullable): uint32 [batch*q_heads, 2048], zero on entry; receives the
- * count of each row's scores per value of the top 11 bits of their order key (a
- * head of a KV head with more than 8 query heads is skipped).  popkv_select uses
- * it to skip its threshold search and zeroes it again.
+ * select_workspace (nullable): a select workspace (popkv_select_workspace_bytes for
+ * batch*q_heads rows, zero-filled once after allocation); the scorer adds each
+ * row's histogram of the top 11 bits of the scores' order keys to it (rows of a
+ * KV head with more than 8 query heads are skipped), and popkv_select with the
+ * same workspace uses and re-zeroes it.
  */
 int popkv_score(const void* queries, int q_dtype, int64_t batch, int64_t q_heads,
                 int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
                 const uint16_t* low, const uint16_t* delta, int64_t kv_heads, int64_t capacity,
                 int cache_per_batch, const int64_t* head_to_kv, int64_t tokens,
                 const int32_t* seq_len, float* scores, int64_t score_stride,
-                uint32_t* score_hist, int flags, popkv_stream_t stream);
+                void* select_workspace, int flags, popkv_stream_t stream);
 
 /*
  * (e) Per-row top-(budget-1) with the newest token reserved.  Replaces
@@ -128,13 +129,18 @@ int popkv_score(const void* queries, int q_dtype, int64_t batch, int64_t q_heads
  * of an attention workspace (see popkv_sparse_attention_masks): row r = b*QH + qh
  * sets bit qh % heads_per_kv of token t in mask row b*(QH/heads_per_kv) + qh/heads_per_kv,
  * with rows_per_seq = QH.  popkv_sparse_attention_premasked then skips its own scatter.
- * score_hist (nullable): the histogram popkv_score wrote for these rows; used when
- * its row total equals L (else ignored), and zeroed for the next step.
+ * select_workspace (nullable, select_workspace_bytes long): the workspace popkv_score
+ * filled for these rows.  With it, the selection runs as two kernels spread over the
+ * whole GPU and leaves the workspace ready for the next step.  A histogram row
+ * that does not add up to L is ignored (the result is the same, only slower).
+ * Calls that share a select workspace must not overlap on the GPU.
  */
+size_t popkv_select_workspace_bytes(int64_t rows, int64_t tokens);
 int popkv_select(const float* scores, int64_t rows, int64_t score_stride, int64_t tokens,
                  const int32_t* seq_len, int64_t rows_per_seq, int64_t budget,
                  int32_t* indices, uint16_t* head_masks, int64_t mask_stride,
-                 int64_t heads_per_kv, uint32_t* score_hist, popkv_stream_t stream);
+                 int64_t heads_per_kv, void* select_workspace, size_t select_workspace_bytes,
+                 popkv_stream_t stream);
 
 /*
  * (f) Fused gather + exact split-K decode attention.  Replaces gather_selected_kv +

@@ -60,7 +60,7 @@ def test_pack_rejects_bad_dtype_and_head_dim(lib):
 def test_select_rejects_budget_one(lib):
     dummy = ctypes.c_void_p(16)
     rc = lib.popkv_select(dummy, *_i64(4, 100, 100), None, ctypes.c_int64(0), ctypes.c_int64(1),
-                          dummy, None, ctypes.c_int64(0), ctypes.c_int64(0), None, None)
+                          dummy, None, ctypes.c_int64(0), ctypes.c_int64(0), None, ctypes.c_size_t(0), None)
     assert rc == 1
 
 
