@@ -167,7 +167,8 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     group = None
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(minutes=5))
         group = dist.group.WORLD
     layers, L0, budget = args.layers, args.context, args.budget
     B = world  # weak scaling: one sequence per GPU, sharded by KV head
@@ -378,8 +379,13 @@ def run_ours(args):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        # Tearing NCCL down while captured graphs still reference its communicator can
+        # block; every rank has finished its collectives, so drop the graphs and leave.
+        stack.graph = None
+        torch.cuda.synchronize()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 def run_reference(args):
