@@ -165,6 +165,10 @@ template <int THREADS>
 __device__ void find_bin(SelectShared& sh, uint32_t remaining) {
     constexpr int kPer = kBins / THREADS;
     const int tid = threadIdx.x;
+    if (tid == 0) {  // a bin is always found when remaining <= total; keep indices in range otherwise
+        sh.sel_bin = 0u;
+        sh.sel_above = 0u;
+    }
     uint32_t local = 0u;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) local += sh.hist[tid * kPer + j];
