@@ -25,6 +25,8 @@
 // buffer holds (heavy ties), the radix select and ranking run over the whole row
 // instead: slower, same result.  Optionally the selection is also OR-ed into the
 // per-KV-head token bitmask the fused attention consumes.  No CTA waits on another.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace popkv {
@@ -42,7 +44,7 @@ constexpr int kRowThreads = 1024;
 // records clock64() at the phase boundaries into a device array of 16 per row.
 #ifdef POPKV_SELECT_PROFILE
 __device__ long long g_select_marks[4096 * 16];
-#define SEL_MARK(i) do { if (threadIdx.x == 0) g_select_marks[blockIdx.x * 16 + (i)] = clock64(); } while (0)
+#define SEL_MARK(i) do { if (threadIdx.x == 0) g_select_marks[(blockIdx.y * gridDim.x + blockIdx.x) * 16 + (i)] = clock64(); } while (0)
 #else
 #define SEL_MARK(i) do { } while (0)
 #endif
@@ -584,6 +586,292 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_finish_kernel(SelectArg
     SEL_MARK(4);
 }
 
+
+// ------------------------------- workspace path: one cluster of C CTAs per row
+// For rows of up to C * kRowThreads * kRowMaxPer tokens.  CTA c of a row's cluster
+// stages the order keys of the row's c-th slice in shared memory with coalesced
+// 16-byte loads (from L2, where the scorer left them); thread t then owns the `per`
+// consecutive keys from t * per on (per odd: the strided shared-memory reads are free
+// of bank conflicts).  The scorer's histogram fixes the top digit in every CTA alike;
+// digits 2 and 3 take a local shared-memory histogram per CTA, which one warp per CTA
+// reduces over the cluster by reading its peers' per-lane sums and then the 64 bins
+// that hold the threshold (distributed shared memory, no remote atomics).  The picks
+// are ranked by a block scan of packed (> thr, == thr) per-thread counts plus the
+// totals of the lower-ranked CTAs, and written in index order.
+namespace cg = cooperative_groups;
+constexpr int kRowMaxPer = 45;
+
+// Histogram bin b lives at b + b / 64: a lane scanning 64 consecutive bins then
+// reads a different bank from its neighbours.
+constexpr int kPaddedBins = kBins + kBins / 64;
+__device__ __forceinline__ int hidx(uint32_t b) { return static_cast<int>(b + (b >> 6)); }
+
+struct RowShared {
+    uint32_t hist[3][kPaddedBins];  // top digit, digit 2, digit 3 (this CTA's counts)
+    uint32_t lane_sum[3][32];  // per-lane sums of each histogram, read by peers
+    uint32_t wsum[32];
+    uint32_t total;            // this CTA's packed (> thr) << 16 | (== thr), read by peers
+    uint32_t sel_bin, sel_above, count;
+    uint32_t base_gt, base_eq;
+};
+
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// Where the running count from the top reaches `remaining` in the sum over the
+// cluster's C copies of sh.hist[slot] (nbins = 2048 or 1024): sh.sel_bin,
+// sh.sel_above (count above the bin) and sh.count (all bins).  Called by every
+// thread after its CTA's histogram is complete; includes the cluster barrier that
+// publishes the histograms.
+template <int C>
+__device__ void cluster_find_bin(RowShared& sh, int slot, int nbins, uint32_t remaining) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int per = nbins / 32;  // bins per lane at level 1 (64 or 32)
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t* h = sh.hist[slot] + hidx(lane * per);  // per <= 64: no padding inside
+        uint32_t l0 = 0u, l1 = 0u;
+#pragma unroll 8
+        for (int j = 0; j < per; j += 2) {
+            l0 += h[j];
+            l1 += h[j + 1];
+        }
+        sh.lane_sum[slot][lane] = l0 + l1;
+    }
+    if constexpr (C > 1) { cluster_arrive(); cluster_wait(); } else { __syncthreads(); }
+    SEL_MARK(5 + slot);
+    if (warp == 0) {
+        cg::cluster_group cluster = cg::this_cluster();
+        uint32_t local = 0u;
+#pragma unroll
+        for (int q = 0; q < C; ++q) {
+            const RowShared* peer = C > 1 ? cluster.map_shared_rank(&sh, q) : &sh;
+            local += peer->lane_sum[slot][lane];
+        }
+        uint32_t suffix = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_down_sync(0xffffffffu, suffix, o);
+            if (lane + o < 32) suffix += y;
+        }
+        const uint32_t total = __shfl_sync(0xffffffffu, suffix, 0);
+        const unsigned hit = __ballot_sync(0xffffffffu, suffix - local < remaining && suffix >= remaining);
+        const int l1 = hit ? __ffs(hit) - 1 : 0;
+        const uint32_t above1 = __shfl_sync(0xffffffffu, suffix - local, l1);
+        // Level 2: lane l takes bins l1 * per + [l * sub, l * sub + sub).
+        const int sub = per / 32;  // 2 or 1
+        const int b0 = l1 * per + lane * sub;
+        uint32_t c0 = 0u, c1 = 0u;
+#pragma unroll
+        for (int q = 0; q < C; ++q) {
+            const RowShared* peer = C > 1 ? cluster.map_shared_rank(&sh, q) : &sh;
+            c0 += peer->hist[slot][hidx(b0)];
+            if (sub == 2) c1 += peer->hist[slot][hidx(b0 + 1)];
+        }
+        const uint32_t l2 = c0 + c1;
+        uint32_t s2 = l2;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_down_sync(0xffffffffu, s2, o);
+            if (lane + o < 32) s2 += y;
+        }
+        const uint32_t ab = above1 + s2 - l2;  // count above this lane's bins
+        if (lane == 0) {
+            sh.count = total;
+            if (!hit) { sh.sel_bin = 0u; sh.sel_above = 0u; }
+        }
+        if (hit && ab < remaining && ab + l2 >= remaining) {  // exactly one lane
+            if (sub == 2 && ab + c1 >= remaining) { sh.sel_bin = b0 + 1; sh.sel_above = ab; }
+            else { sh.sel_bin = b0; sh.sel_above = ab + (sub == 2 ? c1 : 0u); }
+        }
+    }
+    __syncthreads();
+}
+
+template <int C>
+__global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a, int per) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ __align__(16) RowShared sh;
+    extern __shared__ __align__(16) uint32_t s_keys[];  // [kRowThreads * per]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int crank = C > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
+    const int64_t row = blockIdx.y;
+    const int64_t L = row_length(a, row);
+    const int64_t k = a.budget - 1 < L ? a.budget - 1 : L;
+    const RowOut r = row_output(a, row);
+    // This CTA's slice [lo, lo + n); slice starts are multiples of 4 tokens.
+    const int64_t chunk = ((L + C - 1) / C + 3) / 4 * 4;
+    const int64_t lo = imin64(static_cast<int64_t>(crank) * chunk, L);
+    const int n = static_cast<int>(imin64(lo + chunk, L) - lo);
+    uint32_t* hrow = a.hist + row * kBins;
+    SEL_MARK(0);
+
+    // Newest token, padding, and the all/nothing cases (uniform over the cluster).
+    if (crank == 0) {
+        if (tid == 0) {
+            if (r.out) r.out[k] = static_cast<int32_t>(L);
+            if (r.mask_words) atomicOr(r.mask_words + (L >> 1), r.bit << ((L & 1) * 16));
+        }
+        if (r.out)
+            for (int64_t j = k + 1 + tid; j < a.budget; j += kRowThreads) r.out[j] = -1;
+    }
+    if (k == 0 || k == L) {
+        if (k == L)
+            for (int i = tid; i < n; i += kRowThreads) {
+                const int32_t t = static_cast<int32_t>(lo + i);
+                if (r.out) r.out[t] = t;
+                if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
+            }
+        if constexpr (C > 1) { cluster_arrive(); cluster_wait(); }  // every CTA has read the histogram
+        if (crank == 0)
+            for (int i = tid; i < kBins; i += kRowThreads) hrow[i] = 0u;
+        return;
+    }
+
+    // 1. The slice's keys into shared memory, the scorer's histogram beside them.
+    const float* src = a.scores + row * a.stride + lo;
+    if (a.vec) {
+        const int n4 = n >> 2;
+        for (int i = tid; i < n4; i += kRowThreads) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
+            reinterpret_cast<uint4*>(s_keys)[i] =
+                make_uint4(order_key(v.x), order_key(v.y), order_key(v.z), order_key(v.w));
+        }
+        for (int i = (n4 << 2) + tid; i < n; i += kRowThreads) s_keys[i] = order_key(__ldg(src + i));
+    } else {
+        for (int i = tid; i < n; i += kRowThreads) s_keys[i] = order_key(__ldg(src + i));
+    }
+    for (int i = tid; i < kPaddedBins; i += kRowThreads) {
+        sh.hist[1][i] = 0u;
+        sh.hist[2][i] = 0u;
+        if (i % 65 == 64) sh.hist[0][i] = 0u;  // padding slots
+    }
+    for (int i = tid; i < kBins; i += kRowThreads) sh.hist[0][hidx(i)] = __ldcg(hrow + i);
+    const int first = tid * per;
+    const int nvalid = n - first <= 0 ? 0 : (n - first < per ? n - first : per);
+    const uint32_t* mine = s_keys + first;
+    __syncthreads();
+
+    // 2. Top digit: the scorer's histogram when it counted this row's L scores (the
+    // same answer in every CTA of the cluster), else counted here.
+    if (warp == 0) {
+        uint32_t local = 0u;
+#pragma unroll 8
+        for (int i = lane; i < kPaddedBins; i += 32) local += sh.hist[0][i];  // padding is 0
+        local = __reduce_add_sync(0xffffffffu, local);
+        if (lane == 0) sh.count = local;
+    }
+    __syncthreads();
+    uint32_t remaining = static_cast<uint32_t>(k);
+    if (sh.count == static_cast<uint32_t>(L)) {
+        cluster_find_bin<1>(sh, 0, kBins, remaining);  // local: every CTA holds the totals
+    } else {
+        for (int i = tid; i < kPaddedBins; i += kRowThreads) sh.hist[0][i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < n; i += kRowThreads) {
+            const uint32_t d = s_keys[i] >> 21;
+            const unsigned peers = __match_any_sync(__activemask(), d);
+            if (lane == __ffs(peers) - 1) atomicAdd(&sh.hist[0][hidx(d)], __popc(peers));
+        }
+        cluster_find_bin<C>(sh, 0, kBins, remaining);
+    }
+    SEL_MARK(1);
+    uint32_t prefix = sh.sel_bin << 21;
+    remaining -= sh.sel_above;
+
+    // 3. Digits 2 (bits 20..10) and 3 (bits 9..0) over the keys left in the bin.
+    for (int j = 0; j < nvalid; ++j) {
+        const uint32_t x = mine[j];
+        if ((x >> 21) == (prefix >> 21)) atomicAdd(&sh.hist[1][hidx((x >> 10) & 0x7ffu)], 1u);
+    }
+    cluster_find_bin<C>(sh, 1, kBins, remaining);
+    // Every CTA of the cluster has now read the scorer's histogram: zero it for the next step.
+    if (crank == 0)
+        for (int i = tid; i < kBins; i += kRowThreads) hrow[i] = 0u;
+    prefix |= sh.sel_bin << 10;
+    remaining -= sh.sel_above;
+    SEL_MARK(2);
+    for (int j = 0; j < nvalid; ++j) {
+        const uint32_t x = mine[j];
+        if ((x >> 10) == (prefix >> 10)) atomicAdd(&sh.hist[2][hidx(x & 0x3ffu)], 1u);
+    }
+    cluster_find_bin<C>(sh, 2, 1024, remaining);
+    const uint32_t thr = prefix | sh.sel_bin;
+    const uint32_t need = remaining - sh.sel_above;
+    SEL_MARK(3);
+
+    // 4. Rank: (> thr) << 16 | (== thr) counts per thread (slice totals < 2^16), one
+    // exclusive block scan, the lower-ranked CTAs' totals, then each thread writes
+    // its picks in index order.
+    uint32_t cnt = 0u;
+    for (int j = 0; j < nvalid; ++j) {
+        const uint32_t x = mine[j];
+        cnt += x > thr ? 0x10000u : (x == thr ? 1u : 0u);
+    }
+    uint32_t incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) sh.wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t v = sh.wsum[lane];
+        uint32_t x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        sh.wsum[lane] = x - v;
+        if (lane == 31) sh.total = x;
+    }
+    SEL_MARK(8);
+    if constexpr (C > 1) {
+        cluster_arrive();
+        cluster_wait();
+        SEL_MARK(9);
+        if (tid == 0) {
+            cg::cluster_group cluster = cg::this_cluster();
+            uint32_t g = 0u, e = 0u;
+            for (int q = 0; q < crank; ++q) {
+                const uint32_t t = cluster.map_shared_rank(&sh, q)->total;
+                g += t >> 16;
+                e += t & 0xffffu;
+            }
+            sh.base_gt = g;
+            sh.base_eq = e;
+        }
+        cluster_arrive();  // this CTA is done reading its peers
+    } else if (tid == 0) {
+        sh.base_gt = 0u;
+        sh.base_eq = 0u;
+    }
+    __syncthreads();
+    const uint32_t before = incl - cnt + sh.wsum[warp];
+    uint32_t gb = sh.base_gt + (before >> 16), eb = sh.base_eq + (before & 0xffffu);
+    if (cnt != 0u) {
+        for (int j = 0; j < nvalid; ++j) {
+            const uint32_t x = mine[j];
+            if (x > thr || (x == thr && eb < need)) {
+                const int32_t t = static_cast<int32_t>(lo + first + j);
+                if (r.out) r.out[gb + min(eb, need)] = t;
+                if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
+            }
+            gb += x > thr;
+            eb += x == thr;
+        }
+    }
+    SEL_MARK(4);
+    if constexpr (C > 1) cluster_wait();  // peers are done reading this CTA's shared memory
+}
+
 }  // namespace
 }  // namespace popkv
 
@@ -643,6 +931,29 @@ extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_str
         a.ckey = reinterpret_cast<uint32_t*>(base + w.ckey);
         a.cidx = reinterpret_cast<int32_t*>(base + w.cidx);
         a.tokens_pad = w.tokens_pad;
+        // Cluster size: the smallest power of two whose slices fit shared memory,
+        // raised while the rows still leave SMs idle.
+        int C = 1;
+        while (C < 8 && (tokens + C - 1) / C > (int64_t)kRowThreads * kRowMaxPer) C *= 2;
+        while (C < 8 && rows * C * 2 <= num_sms() && (tokens + 2 * C - 1) / (2 * C) >= 2048) C *= 2;
+        const int64_t chunk = ((tokens + C - 1) / C + 3) / 4 * 4;
+        if (chunk <= (int64_t)kRowThreads * kRowMaxPer && rows <= 65535) {
+            const int per = (int)((chunk + kRowThreads - 1) / kRowThreads) | 1;  // odd
+            const size_t smem_keys = (size_t)per * kRowThreads * 4;
+            auto go = [&](auto kern) {
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_keys);
+                if (C > 1) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+                launch_pdl_cluster(kern, dim3((unsigned)C, (unsigned)rows), dim3(kRowThreads), smem_keys,
+                                   st, (unsigned)C, a, per);
+            };
+            switch (C) {
+                case 1: go(select_row_kernel<1>); break;
+                case 2: go(select_row_kernel<2>); break;
+                case 4: go(select_row_kernel<4>); break;
+                default: go(select_row_kernel<8>); break;
+            }
+            return check_launch("popkv_select (row)");
+        }
         const int64_t chunks = (tokens + kChunk - 1) / kChunk;
         if (chunks > 0) {
             launch_pdl(select_candidates_kernel, dim3((unsigned)chunks, (unsigned)rows), dim3(kChunkThreads), 0, st, a);

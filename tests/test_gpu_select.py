@@ -21,6 +21,13 @@ def _check(scores: torch.Tensor, budget: int, lengths=None, rows_per_seq=0):
     per_row = None if lengths is None else np.repeat(lengths, rows_per_seq)[:rows]
     ref = O.select(scores.numpy(), budget=budget, lengths=per_row)
     np.testing.assert_array_equal(got, ref)
+    # The select-workspace path with an empty histogram (the top digit is then
+    # counted inside select) gives the same rows and leaves the histogram zeroed.
+    hist = pk.new_select_workspace(rows, tokens, DEV)
+    got_ws = pk.select(scores.to(DEV), budget=budget, tokens=tokens, seq_len=sl,
+                       rows_per_seq=rows_per_seq, hist=hist).cpu().numpy()
+    np.testing.assert_array_equal(got_ws, ref)
+    assert int(hist[: rows * 2048 * 4].abs().sum()) == 0
     return got
 
 
@@ -98,3 +105,13 @@ def test_select_with_score_histogram_is_exact(G, L):
         torch.testing.assert_close(got, ref, rtol=0, atol=0)
         assert int(hist[: QH * 2048 * 4].abs().sum()) == 0
         np.testing.assert_array_equal(ref.cpu().numpy(), O.select(scores.view(QH, L).cpu().numpy(), budget=budget))
+
+
+@pytest.mark.parametrize("L,budget", [(3001, 2990), (33001, 33000), (40960, 40000)])
+def test_select_threshold_among_negative_infinities(L, budget):
+    """The k-th largest score is -inf (the lowest key bin): padding positions past L
+    must not be counted as -inf scores."""
+    g = torch.Generator().manual_seed(L)
+    scores = torch.randn(3, L, generator=g)
+    scores[:, ::2] = float("-inf")
+    _check(scores, budget)
