@@ -47,6 +47,12 @@ __device__ unsigned long long g_attn_marks[65536 * 8];
 #else
 #define ATTN_MARK(i) do { } while (0)
 #endif
+#ifdef POPKV_ATTN_PROFILE
+__device__ unsigned long long g_comb_marks[65536 * 2];
+#define COMB_MARK(i) do { if (threadIdx.x == 0) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_comb_marks[blockIdx.x * 2 + (i)] = t; } } while (0)
+#else
+#define COMB_MARK(i) do { } while (0)
+#endif
 
 struct AttnParams {
     const void* q;
@@ -177,62 +183,65 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
 
 // ----------------------------------------------------------------- combine
 // One CTA per (sequence, query head): merges the S segment partials (max, sum,
-// acc) into the output.  All S loads of a channel are independent, so the merge
-// costs a few L2 round trips.
+// acc) into the output.  Every warp walks the splits in chunks of 32 with an online
+// rescale (one max, one sum per chunk by warp shuffles, no block barrier), and all
+// loads of a chunk -- max, sum and the thread's accumulator channels -- are issued
+// together, so a chunk costs one L2 round trip.
 template <typename T>
 __global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
     pdl_trigger();
     pdl_wait();
-    __shared__ float s_w[kMaxSplits];
-    __shared__ float s_red[2][4];
+    COMB_MARK(0);
     const int64_t row = blockIdx.x;  // b*QH + qh
-    const int S = p.S;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float mx = -INFINITY;
-    for (int s = tid; s < S; s += blockDim.x) {
-        s_w[s] = __ldcg(p.ws_m + row * S + s);
-        mx = fmaxf(mx, s_w[s]);
-    }
+    const int S = p.S, D = p.D;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const float* mrow = p.ws_m + row * S;
+    const float* lrow = p.ws_l + row * S;
+    const float* arow = p.ws_acc + row * static_cast<int64_t>(S) * D;
+    const int d0 = tid, d1 = tid + 128;  // head_dim <= 256
+    float M = -INFINITY, lsum = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+        const int n = S - s0 < 32 ? S - s0 : 32;
+        const float m_l = lane < n ? __ldcg(mrow + s0 + lane) : -INFINITY;
+        const float l_l = lane < n ? __ldcg(lrow + s0 + lane) : 0.0f;
+        float a0[32], a1[32];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) s_red[0][warp] = mx;
-    __syncthreads();
-    const float M = fmaxf(fmaxf(s_red[0][0], s_red[0][1]), fmaxf(s_red[0][2], s_red[0][3]));
-    float lsum = 0.0f;
-    for (int s = tid; s < S; s += blockDim.x) {
-        const float m = s_w[s];
-        const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
-        s_w[s] = w;
-        lsum += w * __ldcg(p.ws_l + row * S + s);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    if (lane == 0) s_red[1][warp] = lsum;
-    __syncthreads();
-    const float inv = 1.0f / (s_red[1][0] + s_red[1][1] + s_red[1][2] + s_red[1][3]);
-    T* out = static_cast<T*>(p.out);
-    for (int d = tid; d < p.D; d += blockDim.x) {
-        const float* acc = p.ws_acc + row * S * p.D + d;
-        float o0 = 0.0f, o1 = 0.0f;
-        int s = 0;
-        for (; s + 8 <= S; s += 8) {
-            float a[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) a[j] = __ldcg(acc + static_cast<int64_t>(s + j) * p.D);
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-                o0 = fmaf(s_w[s + j], a[j], o0);
-                o1 = fmaf(s_w[s + j + 1], a[j + 1], o1);
-            }
+        for (int j = 0; j < 32; ++j) {
+            const float* src = arow + static_cast<int64_t>(s0 + j) * D;
+            a0[j] = (j < n && d0 < D) ? __ldcg(src + d0) : 0.0f;
+            a1[j] = (j < n && d1 < D) ? __ldcg(src + d1) : 0.0f;
         }
-        for (; s < S; ++s) o0 = fmaf(s_w[s], __ldcg(acc + static_cast<int64_t>(s) * p.D), o0);
-        out[row * p.D + d] = from_float<T>((o0 + o1) * inv);
+        float cmax = m_l;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+        const float m_new = fmaxf(M, cmax);
+        if (m_new == -INFINITY) continue;  // uniform: no token in these splits yet
+        const float scale = exp2f(M - m_new);  // 0 while M is still -inf
+        o0 *= scale;
+        o1 *= scale;
+        lsum *= scale;
+        const float w_l = m_l == -INFINITY ? 0.0f : exp2f(m_l - m_new);
+        float wl = w_l * l_l;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wl += __shfl_xor_sync(0xffffffffu, wl, o);
+        lsum += wl;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float w = __shfl_sync(0xffffffffu, w_l, j);
+            o0 = fmaf(w, a0[j], o0);
+            o1 = fmaf(w, a1[j], o1);
+        }
+        M = m_new;
     }
+    const float inv = 1.0f / lsum;
+    T* out = static_cast<T*>(p.out);
+    if (d0 < D) out[row * D + d0] = from_float<T>(o0 * inv);
+    if (d1 < D) out[row * D + d1] = from_float<T>(o1 * inv);
+    COMB_MARK(1);
 }
 
 // -------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+__device__ __forceinline__ void cp_async16_s(uint32_t s, const void* gmem, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
                  "r"(src_bytes));
 }
@@ -358,36 +367,35 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
     const int64_t cache_head = (p.per_batch ? static_cast<int64_t>(b) * p.KVH : 0) + kvh;
     const int64_t cur_row = (static_cast<int64_t>(b) * p.KVH + kvh) * D;
     T* ring = reinterpret_cast<T*>(work) + warp * kStages * 2 * kTileRows * LDS;
+    const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+    const T* kb = kc + cache_head * p.kv_cap * D;
+    const T* vb = vc + cache_head * p.kv_cap * D;
+    const T* ckr = cur_k != nullptr ? cur_k + cur_row : nullptr;
+    const T* cvr = cur_v != nullptr ? cur_v + cur_row : nullptr;
+    const int Li = static_cast<int>(L);
 
+    // Copies of tile `tile` (16 union rows of K and V) into ring stage `st`; rows past
+    // the union are zero-filled.
     auto issue = [&](int tile, int st) {
-        T* kd = ring + st * 2 * kTileRows * LDS;
-        T* vd = kd + kTileRows * LDS;
         constexpr int CPR = D * (int)sizeof(T) / 16;
         constexpr int EPC = 16 / (int)sizeof(T);
+        constexpr uint32_t kStageBytes = 2 * kTileRows * LDS * sizeof(T);
+        const uint32_t kd = ring_s + st * kStageBytes;
+        const uint32_t vd = kd + kTileRows * LDS * sizeof(T);
 #pragma unroll
         for (int c = lane; c < kTileRows * CPR; c += 32) {
             const int r = c / CPR;
             const int ch = c - r * CPR;
             const int e = tile * kTileRows + r;
-            const T* ks = kc;
-            const T* vs = vc;
-            int bytes = 0;
-            if (e < n_union) {
-                const int64_t t = s_tok[e];
-                bytes = 16;
-                if (t == L && cur_k != nullptr) {
-                    ks = cur_k + cur_row;
-                    vs = cur_v + cur_row;
-                } else {
-                    ks = kc + (cache_head * p.kv_cap + t) * D;
-                    vs = vc + (cache_head * p.kv_cap + t) * D;
-                }
-                ks += ch * EPC;
-                vs += ch * EPC;
-            }
+            const bool in = e < n_union;
+            const int t = in ? s_tok[e] : 0;
+            const bool cur = t == Li && ckr != nullptr;
+            const T* ks = (cur ? ckr : kb + static_cast<int64_t>(t) * D) + ch * EPC;
+            const T* vs = (cur ? cvr : vb + static_cast<int64_t>(t) * D) + ch * EPC;
             const int pch = Plan::SWZ ? (ch ^ (r & 7)) : ch;
-            cp_async16(kd + r * LDS + pch * EPC, ks, bytes);
-            cp_async16(vd + r * LDS + pch * EPC, vs, bytes);
+            const uint32_t off = static_cast<uint32_t>((r * LDS + pch * EPC) * sizeof(T));
+            cp_async16_s(kd + off, ks, in ? 16 : 0);
+            cp_async16_s(vd + off, vs, in ? 16 : 0);
         }
     };
 
@@ -711,6 +719,9 @@ using namespace popkv;
 #ifdef POPKV_ATTN_PROFILE
 extern "C" int attn_read_marks(unsigned long long* host, int n) {
     return (int)cudaMemcpyFromSymbol(host, g_attn_marks, n * sizeof(unsigned long long));
+}
+extern "C" int comb_read_marks(unsigned long long* host, int n) {
+    return (int)cudaMemcpyFromSymbol(host, g_comb_marks, n * sizeof(unsigned long long));
 }
 #endif
 
