@@ -187,57 +187,82 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
 // rescale (one max, one sum per chunk by warp shuffles, no block barrier), and all
 // loads of a chunk -- max, sum and the thread's accumulator channels -- are issued
 // together, so a chunk costs one L2 round trip.
-template <typename T>
+template <typename T, int CH>  // CH = splits per chunk: 64 (head_dim <= 128) or 32
 __global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
     pdl_trigger();
     pdl_wait();
     COMB_MARK(0);
-    const int64_t row = blockIdx.x;  // b*QH + qh
+    constexpr int DPT = CH == 64 ? 1 : 2;  // channels per thread (tid, tid + 128)
+    const int64_t row = blockIdx.x;        // b*QH + qh
     const int S = p.S, D = p.D;
     const int tid = threadIdx.x, lane = tid & 31;
     const float* mrow = p.ws_m + row * S;
     const float* lrow = p.ws_l + row * S;
     const float* arow = p.ws_acc + row * static_cast<int64_t>(S) * D;
-    const int d0 = tid, d1 = tid + 128;  // head_dim <= 256
-    float M = -INFINITY, lsum = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 32) {
-        const int n = S - s0 < 32 ? S - s0 : 32;
-        const float m_l = lane < n ? __ldcg(mrow + s0 + lane) : -INFINITY;
-        const float l_l = lane < n ? __ldcg(lrow + s0 + lane) : 0.0f;
-        float a0[32], a1[32];
+    float M = -INFINITY, lsum = 0.0f, o[DPT];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const float* src = arow + static_cast<int64_t>(s0 + j) * D;
-            a0[j] = (j < n && d0 < D) ? __ldcg(src + d0) : 0.0f;
-            a1[j] = (j < n && d1 < D) ? __ldcg(src + d1) : 0.0f;
+    for (int c = 0; c < DPT; ++c) o[c] = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += CH) {
+        const int n = S - s0 < CH ? S - s0 : CH;
+        float m_l[CH / 32], l_l[CH / 32];
+#pragma unroll
+        for (int h = 0; h < CH / 32; ++h) {
+            const int j = h * 32 + lane;
+            m_l[h] = j < n ? __ldcg(mrow + s0 + j) : -INFINITY;
+            l_l[h] = j < n ? __ldcg(lrow + s0 + j) : 0.0f;
         }
-        float cmax = m_l;
+        float a[DPT][CH];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+        for (int j = 0; j < CH; ++j) {
+            const float* src = arow + static_cast<int64_t>(s0 + j) * D;
+#pragma unroll
+            for (int c = 0; c < DPT; ++c) {
+                const int d = tid + 128 * c;
+                a[c][j] = (j < n && d < D) ? __ldcg(src + d) : 0.0f;
+            }
+        }
+        float cmax = m_l[0];
+#pragma unroll
+        for (int h = 1; h < CH / 32; ++h) cmax = fmaxf(cmax, m_l[h]);
+#pragma unroll
+        for (int x = 16; x > 0; x >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, x));
         const float m_new = fmaxf(M, cmax);
         if (m_new == -INFINITY) continue;  // uniform: no token in these splits yet
         const float scale = exp2f(M - m_new);  // 0 while M is still -inf
-        o0 *= scale;
-        o1 *= scale;
         lsum *= scale;
-        const float w_l = m_l == -INFINITY ? 0.0f : exp2f(m_l - m_new);
-        float wl = w_l * l_l;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) wl += __shfl_xor_sync(0xffffffffu, wl, o);
+        for (int c = 0; c < DPT; ++c) o[c] *= scale;
+        float w_l[CH / 32], wl = 0.0f;
+#pragma unroll
+        for (int h = 0; h < CH / 32; ++h) {
+            w_l[h] = m_l[h] == -INFINITY ? 0.0f : exp2f(m_l[h] - m_new);
+            wl = fmaf(w_l[h], l_l[h], wl);
+        }
+#pragma unroll
+        for (int x = 16; x > 0; x >>= 1) wl += __shfl_xor_sync(0xffffffffu, wl, x);
         lsum += wl;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const float w = __shfl_sync(0xffffffffu, w_l, j);
-            o0 = fmaf(w, a0[j], o0);
-            o1 = fmaf(w, a1[j], o1);
+        for (int j = 0; j < CH; ++j) {
+            const float w = __shfl_sync(0xffffffffu, w_l[j / 32], j & 31);
+#pragma unroll
+            for (int c = 0; c < DPT; ++c) o[c] = fmaf(w, a[c][j], o[c]);
         }
         M = m_new;
     }
     const float inv = 1.0f / lsum;
     T* out = static_cast<T*>(p.out);
-    if (d0 < D) out[row * D + d0] = from_float<T>(o0 * inv);
-    if (d1 < D) out[row * D + d1] = from_float<T>(o1 * inv);
+#pragma unroll
+    for (int c = 0; c < DPT; ++c) {
+        const int d = tid + 128 * c;
+        if (d < D) out[row * D + d] = from_float<T>(o[c] * inv);
+    }
     COMB_MARK(1);
+}
+
+template <typename T>
+void launch_combine(const AttnParams& p, cudaStream_t st) {
+    if (p.D <= 128) launch_pdl(combine_kernel<T, 64>, dim3((unsigned)(p.B * p.QH)), dim3(128), 0, st, p);
+    else launch_pdl(combine_kernel<T, 32>, dim3((unsigned)(p.B * p.QH)), dim3(128), 0, st, p);
 }
 
 // -------------------------------------------------------------- PTX helpers
@@ -692,7 +717,7 @@ int launch_mma(const AttnParams& p, cudaStream_t st) {
     launch_pdl(kern, dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), dim3(kAttnThreads), smem, st, p);
     const int rc = check_launch("popkv_sparse_attention");
     if (rc != POPKV_OK) return rc;
-    launch_pdl(combine_kernel<T>, dim3((unsigned)(p.B * p.QH)), dim3(128), 0, st, p);
+    launch_combine<T>(p, st);
     return check_launch("popkv_sparse_attention (combine)");
 }
 
@@ -707,7 +732,7 @@ int launch_simt(AttnParams p, cudaStream_t st) {
     launch_pdl(kern, dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), dim3(kAttnThreads), smem, st, p);
     const int rc = check_launch("popkv_sparse_attention");
     if (rc != POPKV_OK) return rc;
-    launch_pdl(combine_kernel<T>, dim3((unsigned)(p.B * p.QH)), dim3(128), 0, st, p);
+    launch_combine<T>(p, st);
     return check_launch("popkv_sparse_attention (combine)");
 }
 
