@@ -33,10 +33,6 @@ constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 16;
 constexpr int kSegMax = 2048;   // tokens per segment (multiple of 8)
 constexpr int kTileRows = 16;
-#ifndef POPKV_ATTN_STAGES
-#define POPKV_ATTN_STAGES 3
-#endif
-constexpr int kStages = POPKV_ATTN_STAGES;  // cp.async ring depth per warp
 constexpr int kMaxSplits = 1024;
 
 // Phase timestamps for tuning builds (-DPOPKV_ATTN_PROFILE): thread 0 of each CTA
@@ -113,15 +109,18 @@ __global__ void scatter_kernel(AttnParams p) {
 // Reads the bitmask of tokens [lo, lo+n) (n <= kSegMax, lo multiple of 8), clears
 // it, and writes the selected tokens (ascending) and their head masks to shared
 // memory.  Returns the union size (same value in every thread).
-__device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int n, int* s_tok,
+template <typename TokT>
+__device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int n, TokT* s_tok,
                            uint16_t* s_msk, int* s_scan, bool dense) {
+    // int lists hold token indices; uint16 lists hold offsets from lo (n <= kSegMax).
+    const int64_t tok_base = sizeof(TokT) == 2 ? lo : 0;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
     if (dense) {
         const uint16_t full = static_cast<uint16_t>((1u << p.G) - 1u);
         for (int i = tid; i < n; i += kAttnThreads) {
-            s_tok[i] = static_cast<int>(lo + i);
+            s_tok[i] = static_cast<TokT>(lo + i - tok_base);
             s_msk[i] = full;
         }
         __syncthreads();
@@ -172,7 +171,7 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
         if (m[j]) {
-            s_tok[pos] = static_cast<int>(lo + first + j);
+            s_tok[pos] = static_cast<TokT>(lo + first + j - tok_base);
             s_msk[pos] = m[j];
             ++pos;
         }
@@ -319,6 +318,12 @@ template <> struct MmaOp<__half> {
 };
 
 // Shared-memory plan of the tensor-core kernel (bytes).
+#ifndef POPKV_ATTN_CTAS_PER_SM
+#define POPKV_ATTN_CTAS_PER_SM 3
+#endif
+constexpr int kMmaCtasPerSm = POPKV_ATTN_CTAS_PER_SM;
+constexpr int kMmaStages = kMmaCtasPerSm >= 3 ? 2 : 3;  // cp.async ring depth per warp
+
 template <typename T, int D>
 struct MmaPlan {
     // Rows of 8 or 16 sixteen-byte chunks are stored unpadded with chunk c of row r
@@ -331,24 +336,37 @@ struct MmaPlan {
 #endif
     static constexpr int LDS = SWZ ? D : D + 8;
     static constexpr int kStageBytes = 2 * kTileRows * LDS * (int)sizeof(T);
-    static constexpr int kRingBytes = kAttnWarps * kStages * kStageBytes;
+    static constexpr int kRingBytes = kAttnWarps * kMmaStages * kStageBytes;
     static constexpr int kMergeBytes = kAttnWarps * kMaxGroup * (D + 2) * 4;
     static constexpr int kWorkBytes = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
-    static constexpr int kListBytes = kSegMax * 4 + kSegMax * 2;
+    static constexpr int kListBytes = kSegMax * 2 + kSegMax * 2;  // uint16 offsets + head masks
 };
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnParams p) {
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
+}
+
+// Tokens in M, query heads in N.  Per 16-row tile a warp computes
+// S^T = K_tile Q^T (16 tokens x 8 heads per n-tile, K_tile straight from the ring
+// as the A operand, Q^T preloaded as B fragments), runs the online softmax per head
+// column (reductions over the 8 lanes that share a column), turns P^T into B
+// fragments with movmatrix, and accumulates O^T += V_tile^T P^T (head_dim in M,
+// V^T read with ldmatrix.trans).  NHT = n-tiles of 8 query heads (G <= 8 * NHT).
+template <typename T, int D, int NHT>
+__global__ void __launch_bounds__(kAttnThreads, kMmaCtasPerSm) attention_mma_kernel(AttnParams p) {
     pdl_trigger();
     pdl_wait();
     using Plan = MmaPlan<T, D>;
     constexpr int LDS = Plan::LDS;
-    constexpr int NT8 = D / 8;   // output n-tiles
-    constexpr int KS = D / 16;   // k-steps of QK
+    constexpr int KS = D / 16;   // k-steps of QK^T
+    constexpr int MT = D / 16;   // m-tiles of O^T
+    constexpr int kStages = kMmaStages;
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* work = smem;
-    int* s_tok = reinterpret_cast<int*>(smem + Plan::kWorkBytes);
-    uint16_t* s_msk = reinterpret_cast<uint16_t*>(s_tok + kSegMax);
+    uint16_t* s_tok = reinterpret_cast<uint16_t*>(smem + Plan::kWorkBytes);  // offsets from lo
+    uint16_t* s_msk = s_tok + kSegMax;
     __shared__ int s_scan[kAttnWarps];
 
     const int s = blockIdx.x;
@@ -366,19 +384,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
     ATTN_MARK(0);
     const T* q = static_cast<const T*>(p.q);
     const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
-    // Query fragments (A operand, heads g and g+8), loaded while the union is built.
-    uint32_t qa[KS][4];
-    {
-        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(q + (qrow0 + g) * D);
-        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(q + (qrow0 + g + 8) * D);
-        const bool h0 = g < p.G, h1 = g + 8 < p.G;
+    // Q^T fragments (B operand): head 8 * nh + g, channels 16 kk + 2 tig (+1, +8, +9).
+    uint32_t qb[NHT][KS][2];
+#pragma unroll
+    for (int nh = 0; nh < NHT; ++nh) {
+        const int h = 8 * nh + g;
+        const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + (qrow0 + (h < p.G ? h : 0)) * D);
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-            const int c = (16 * kk + 2 * tig) / 2;
-            qa[kk][0] = h0 ? __ldg(q0 + c) : 0u;
-            qa[kk][1] = h1 ? __ldg(q1 + c) : 0u;
-            qa[kk][2] = h0 ? __ldg(q0 + c + 4) : 0u;
-            qa[kk][3] = h1 ? __ldg(q1 + c + 4) : 0u;
+            qb[nh][kk][0] = h < p.G ? __ldg(qr + 8 * kk + tig) : 0u;
+            qb[nh][kk][1] = h < p.G ? __ldg(qr + 8 * kk + 4 + tig) : 0u;
         }
     }
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
@@ -393,19 +408,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
     const int64_t cur_row = (static_cast<int64_t>(b) * p.KVH + kvh) * D;
     T* ring = reinterpret_cast<T*>(work) + warp * kStages * 2 * kTileRows * LDS;
     const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
-    const T* kb = kc + cache_head * p.kv_cap * D;
-    const T* vb = vc + cache_head * p.kv_cap * D;
+    const T* kb = kc + (cache_head * p.kv_cap + lo) * D;  // row of offset 0
+    const T* vb = vc + (cache_head * p.kv_cap + lo) * D;
     const T* ckr = cur_k != nullptr ? cur_k + cur_row : nullptr;
     const T* cvr = cur_v != nullptr ? cur_v + cur_row : nullptr;
-    const int Li = static_cast<int>(L);
+    const int cur_off = static_cast<int>(L - lo);  // offset of the newest token
 
     // Copies of tile `tile` (16 union rows of K and V) into ring stage `st`; rows past
     // the union are zero-filled.
     auto issue = [&](int tile, int st) {
         constexpr int CPR = D * (int)sizeof(T) / 16;
         constexpr int EPC = 16 / (int)sizeof(T);
-        constexpr uint32_t kStageBytes = 2 * kTileRows * LDS * sizeof(T);
-        const uint32_t kd = ring_s + st * kStageBytes;
+        constexpr uint32_t kStageB = 2 * kTileRows * LDS * sizeof(T);
+        const uint32_t kd = ring_s + st * kStageB;
         const uint32_t vd = kd + kTileRows * LDS * sizeof(T);
 #pragma unroll
         for (int c = lane; c < kTileRows * CPR; c += 32) {
@@ -413,8 +428,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
             const int ch = c - r * CPR;
             const int e = tile * kTileRows + r;
             const bool in = e < n_union;
-            const int t = in ? s_tok[e] : 0;
-            const bool cur = t == Li && ckr != nullptr;
+            const int t = in ? static_cast<int>(s_tok[e]) : 0;
+            const bool cur = t == cur_off && ckr != nullptr;
             const T* ks = (cur ? ckr : kb + static_cast<int64_t>(t) * D) + ch * EPC;
             const T* vs = (cur ? cvr : vb + static_cast<int64_t>(t) * D) + ch * EPC;
             const int pch = Plan::SWZ ? (ch ^ (r & 7)) : ch;
@@ -424,11 +439,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
         }
     };
 
-    float acc[NT8][4];
+    float acc[MT][NHT][4];
 #pragma unroll
-    for (int i = 0; i < NT8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
-    float m_run[2] = {-INFINITY, -INFINITY};
-    float l_run[2] = {0.0f, 0.0f};
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nh = 0; nh < NHT; ++nh) acc[mt][nh][0] = acc[mt][nh][1] = acc[mt][nh][2] = acc[mt][nh][3] = 0.0f;
+    float m_run[NHT][2], l_run[NHT][2];  // heads 8 nh + 2 tig + j (l: this lane's tokens only)
+#pragma unroll
+    for (int nh = 0; nh < NHT; ++nh) {
+        m_run[nh][0] = m_run[nh][1] = -INFINITY;
+        l_run[nh][0] = l_run[nh][1] = 0.0f;
+    }
 
     const int n_tiles = (n_union + kTileRows - 1) / kTileRows;
     const int my_tiles = n_tiles > warp ? (n_tiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
@@ -447,104 +468,106 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
         const T* Ks = ring + (i % kStages) * 2 * kTileRows * LDS;
         const T* Vs = Ks + kTileRows * LDS;
 
-        // S = Q K^T for the tile's 16 rows (two n-tiles of 8 rows).
-        float sc[2][4];
+        // S^T = K Q^T: rows g, g + 8 of the tile, head columns 2 tig, 2 tig + 1.
+        float sc[NHT][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+        for (int nh = 0; nh < NHT; ++nh) sc[nh][0] = sc[nh][1] = sc[nh][2] = sc[nh][3] = 0.0f;
 #pragma unroll
-            for (int k2 = 0; k2 < D / 32; ++k2) {
-                uint32_t bf[4];
-                const int kch = k2 * 4 + (lane >> 3);
-                ldmatrix_x4(bf, Ks + (nt * 8 + (lane & 7)) * LDS +
-                                    (Plan::SWZ ? (kch ^ (lane & 7)) : kch) * 8);
-                MmaOp<T>::run(sc[nt], qa[2 * k2], bf[0], bf[1]);
-                MmaOp<T>::run(sc[nt], qa[2 * k2 + 1], bf[2], bf[3]);
-            }
+        for (int kk = 0; kk < KS; ++kk) {
+            uint32_t a[4];
+            const int r = lane & 15;
+            const int kch = 2 * kk + (lane >> 4);
+            ldmatrix_x4(a, Ks + r * LDS + (Plan::SWZ ? (kch ^ (r & 7)) : kch) * 8);
+#pragma unroll
+            for (int nh = 0; nh < NHT; ++nh) MmaOp<T>::run(sc[nh], a, qb[nh][kk][0], qb[nh][kk][1]);
         }
-        // Mask (head not selecting the row, or padding row) and scale to log2 domain.
-        float x[2][4];
+        const int e0 = tile * kTileRows + g;
+        const uint32_t mk0 = e0 < n_union ? s_msk[e0] : 0u;
+        const uint32_t mk1 = e0 + 8 < n_union ? s_msk[e0 + 8] : 0u;
+        uint32_t pb[NHT][2];
+        bool rescale = false;
+        float corr[NHT][2];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
+        for (int nh = 0; nh < NHT; ++nh) {
+            float pr[4];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int e = tile * kTileRows + nt * 8 + 2 * tig + j;
-                const uint32_t mk = e < n_union ? s_msk[e] : 0u;
-                x[nt][j] = ((mk >> g) & 1u) ? sc[nt][j] * p.sl2 : -INFINITY;
-                x[nt][2 + j] = ((mk >> (g + 8)) & 1u) ? sc[nt][2 + j] * p.sl2 : -INFINITY;
+                const int h = 8 * nh + 2 * tig + j;
+                const float x0 = ((mk0 >> h) & 1u) ? sc[nh][j] * p.sl2 : -INFINITY;      // row g
+                const float x1 = ((mk1 >> h) & 1u) ? sc[nh][2 + j] * p.sl2 : -INFINITY;  // row g + 8
+                float tmax = fmaxf(x0, x1);
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+                const float m_new = fmaxf(m_run[nh][j], tmax);
+                const float cr = (m_new == -INFINITY || m_new == m_run[nh][j]) ? 1.0f
+                                                                               : exp2f(m_run[nh][j] - m_new);
+                const float p0 = x0 == -INFINITY ? 0.0f : exp2f(x0 - m_new);
+                const float p1 = x1 == -INFINITY ? 0.0f : exp2f(x1 - m_new);
+                pr[j] = p0;
+                pr[2 + j] = p1;
+                l_run[nh][j] = fmaf(l_run[nh][j], cr, p0 + p1);
+                m_run[nh][j] = m_new;
+                corr[nh][j] = cr;
+                rescale |= cr != 1.0f;
             }
+            pb[nh][0] = movmatrix_trans(MmaOp<T>::pack(pr[0], pr[1]));  // tokens 0-7
+            pb[nh][1] = movmatrix_trans(MmaOp<T>::pack(pr[2], pr[3]));  // tokens 8-15
         }
-        float pr[2][4];
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-            float tmax = fmaxf(fmaxf(x[0][2 * hh], x[0][2 * hh + 1]), fmaxf(x[1][2 * hh], x[1][2 * hh + 1]));
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-            const float m_new = fmaxf(m_run[hh], tmax);
-            const bool none = m_new == -INFINITY;
-            const float corr = none ? 1.0f : exp2f(m_run[hh] - m_new);
-            float psum = 0.0f;
+            for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const float v = x[nt][2 * hh + j];
-                    const float e = (v == -INFINITY) ? 0.0f : exp2f(v - m_new);
-                    pr[nt][2 * hh + j] = e;
-                    psum += e;
+                for (int nh = 0; nh < NHT; ++nh) {
+                    acc[mt][nh][0] *= corr[nh][0];
+                    acc[mt][nh][1] *= corr[nh][1];
+                    acc[mt][nh][2] *= corr[nh][0];
+                    acc[mt][nh][3] *= corr[nh][1];
                 }
-            }
-            l_run[hh] = l_run[hh] * corr + psum;
-            m_run[hh] = m_new;
-#pragma unroll
-            for (int n8 = 0; n8 < NT8; ++n8) {
-                acc[n8][2 * hh] *= corr;
-                acc[n8][2 * hh + 1] *= corr;
-            }
         }
-        uint32_t pa[4];
-        pa[0] = MmaOp<T>::pack(pr[0][0], pr[0][1]);
-        pa[1] = MmaOp<T>::pack(pr[0][2], pr[0][3]);
-        pa[2] = MmaOp<T>::pack(pr[1][0], pr[1][1]);
-        pa[3] = MmaOp<T>::pack(pr[1][2], pr[1][3]);
-        // O += P V.
+        // O^T += V^T P^T: head_dim rows 16 mt + g (+8), head columns 2 tig (+1).
 #pragma unroll
-        for (int np = 0; np < D / 16; ++np) {
-            uint32_t bf[4];
-            const int vch = np * 2 + (lane >> 4);
-            ldmatrix_x4_trans(bf, Vs + (((lane >> 3) & 1) * 8 + (lane & 7)) * LDS +
-                                      (Plan::SWZ ? (vch ^ (lane & 7)) : vch) * 8);
-            MmaOp<T>::run(acc[2 * np], pa, bf[0], bf[1]);
-            MmaOp<T>::run(acc[2 * np + 1], pa, bf[2], bf[3]);
+        for (int mt = 0; mt < MT; ++mt) {
+            uint32_t a[4];
+            const int r = (lane & 7) + ((lane >> 4) << 3);
+            const int vch = 2 * mt + ((lane >> 3) & 1);
+            ldmatrix_x4_trans(a, Vs + r * LDS + (Plan::SWZ ? (vch ^ (r & 7)) : vch) * 8);
+#pragma unroll
+            for (int nh = 0; nh < NHT; ++nh) MmaOp<T>::run(acc[mt][nh], a, pb[nh][0], pb[nh][1]);
         }
         __syncwarp();
     }
     cp_async_wait<0>();
     ATTN_MARK(2);
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 1);
-        l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 2);
-    }
+    for (int nh = 0; nh < NHT; ++nh)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            l_run[nh][j] += __shfl_xor_sync(0xffffffffu, l_run[nh][j], 4);
+            l_run[nh][j] += __shfl_xor_sync(0xffffffffu, l_run[nh][j], 8);
+            l_run[nh][j] += __shfl_xor_sync(0xffffffffu, l_run[nh][j], 16);
+        }
     __syncthreads();  // ring no longer needed: reuse it for the warp merge
     float* s_wm = reinterpret_cast<float*>(work);            // [warps][16]
     float* s_wl = s_wm + kAttnWarps * kMaxGroup;              // [warps][16]
     float* s_wacc = s_wl + kAttnWarps * kMaxGroup;            // [warps][16][D]
-    if (tig == 0) {
-        s_wm[warp * kMaxGroup + g] = m_run[0];
-        s_wm[warp * kMaxGroup + g + 8] = m_run[1];
-        s_wl[warp * kMaxGroup + g] = l_run[0];
-        s_wl[warp * kMaxGroup + g + 8] = l_run[1];
-    }
 #pragma unroll
-    for (int n8 = 0; n8 < NT8; ++n8) {
-        const int c = n8 * 8 + 2 * tig;
-        float* r0 = s_wacc + (warp * kMaxGroup + g) * D + c;
-        float* r1 = s_wacc + (warp * kMaxGroup + g + 8) * D + c;
-        r0[0] = acc[n8][0];
-        r0[1] = acc[n8][1];
-        r1[0] = acc[n8][2];
-        r1[1] = acc[n8][3];
+    for (int nh = 0; nh < NHT; ++nh) {
+        if (g == 0) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                s_wm[warp * kMaxGroup + 8 * nh + 2 * tig + j] = m_run[nh][j];
+                s_wl[warp * kMaxGroup + 8 * nh + 2 * tig + j] = l_run[nh][j];
+            }
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            float* r0 = s_wacc + (warp * kMaxGroup + 8 * nh + 2 * tig) * D + 16 * mt + g;
+            r0[0] = acc[mt][nh][0];
+            r0[D] = acc[mt][nh][1];
+            r0[8] = acc[mt][nh][2];
+            r0[D + 8] = acc[mt][nh][3];
+        }
     }
     __syncthreads();
     for (int i = tid; i < p.G * D; i += kAttnThreads) {
@@ -570,7 +593,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_mma_kernel(AttnPara
             p.ws_l[prow] = l;
         }
     }
-    __syncthreads();
     ATTN_MARK(3);
 }
 
@@ -699,7 +721,10 @@ WorkspaceLayout layout(int64_t B, int64_t QH, int64_t KVH, int64_t D, int64_t to
 
 int64_t auto_splits(int64_t B, int64_t KVH, int64_t tokens) {
     const int64_t min_s = (tokens + 1 + (kSegMax - 8) - 1) / (kSegMax - 8);
-    const int64_t fill = (2 * 148 + B * KVH - 1) / (B * KVH);
+    // One wave: every CTA resident at once (a partly filled second wave costs a
+    // whole extra segment time).
+    int64_t fill = (int64_t)kMmaCtasPerSm * num_sms() / (B * KVH);
+    if (fill < 1) fill = 1;
     int64_t S = min_s > fill ? min_s : fill;
     const int64_t max_useful = (tokens + 1 + 63) / 64;  // keep >= 64 tokens per segment
     if (S > max_useful && max_useful >= min_s) S = max_useful;
@@ -712,7 +737,7 @@ int launch_mma(const AttnParams& p, cudaStream_t st) {
     using Plan = MmaPlan<T, D>;
     const size_t smem = (size_t)Plan::kWorkBytes + Plan::kListBytes;
     if (smem > 227 * 1024) return fail(POPKV_ERR_UNSUPPORTED, "too many splits for shared memory");
-    auto kern = attention_mma_kernel<T, D>;
+    auto kern = p.G <= 8 ? attention_mma_kernel<T, D, 1> : attention_mma_kernel<T, D, 2>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_pdl(kern, dim3((unsigned)p.S, (unsigned)(p.B * p.KVH)), dim3(kAttnThreads), smem, st, p);
     const int rc = check_launch("popkv_sparse_attention");
