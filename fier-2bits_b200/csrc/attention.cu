@@ -354,9 +354,33 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
 // column (reductions over the 8 lanes that share a column), turns P^T into B
 // fragments with movmatrix, and accumulates O^T += V_tile^T P^T (head_dim in M,
 // V^T read with ldmatrix.trans).  NHT = n-tiles of 8 query heads (G <= 8 * NHT).
+// Q^T fragments (B operand) of the heads 8 nh + g of this CTA's KV head, channels
+// 16 kk + 2 t (+1, +8, +9).  The queries are never written by this library's
+// kernels, so the loads may run before griddepcontrol.wait.
+template <typename T, int D, int NHT>
+__device__ __forceinline__ void prefetch_q_fragments(uint32_t (&qb)[NHT][D / 16][2], const AttnParams& p) {
+    const int b = blockIdx.y / p.KVH;
+    const int kvh = blockIdx.y - b * p.KVH;
+    const int g = (threadIdx.x & 31) >> 2, tig = threadIdx.x & 3;
+    const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
+    const T* q = static_cast<const T*>(p.q);
+#pragma unroll
+    for (int nh = 0; nh < NHT; ++nh) {
+        const int h = 8 * nh + g;
+        const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + (qrow0 + (h < p.G ? h : 0)) * D);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+            qb[nh][kk][0] = h < p.G ? __ldg(qr + 8 * kk + tig) : 0u;
+            qb[nh][kk][1] = h < p.G ? __ldg(qr + 8 * kk + 4 + tig) : 0u;
+        }
+    }
+}
+
 template <typename T, int D, int NHT>
 __global__ void __launch_bounds__(kAttnThreads, kMmaCtasPerSm) attention_mma_kernel(AttnParams p) {
     pdl_trigger();
+    uint32_t qb[NHT][D / 16][2];
+    prefetch_q_fragments<T, D, NHT>(qb, p);
     pdl_wait();
     using Plan = MmaPlan<T, D>;
     constexpr int LDS = Plan::LDS;
@@ -382,20 +406,7 @@ __global__ void __launch_bounds__(kAttnThreads, kMmaCtasPerSm) attention_mma_ker
     const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
     const int64_t hi = imin64(lo + seg, L + 1);
     ATTN_MARK(0);
-    const T* q = static_cast<const T*>(p.q);
     const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
-    // Q^T fragments (B operand): head 8 * nh + g, channels 16 kk + 2 tig (+1, +8, +9).
-    uint32_t qb[NHT][KS][2];
-#pragma unroll
-    for (int nh = 0; nh < NHT; ++nh) {
-        const int h = 8 * nh + g;
-        const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + (qrow0 + (h < p.G ? h : 0)) * D);
-#pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-            qb[nh][kk][0] = h < p.G ? __ldg(qr + 8 * kk + tig) : 0u;
-            qb[nh][kk][1] = h < p.G ? __ldg(qr + 8 * kk + 4 + tig) : 0u;
-        }
-    }
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
                                     p.dense != 0);
     ATTN_MARK(1);

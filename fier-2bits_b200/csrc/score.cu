@@ -78,14 +78,15 @@ struct PackedRow {
 };
 
 template <typename TQ, int W, bool VEC>
-__global__ void __launch_bounds__(kScoreThreads)
+__global__ void __launch_bounds__(kScoreThreads, 2)
 score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
              const int32_t* __restrict__ k_sign, const int32_t* __restrict__ k_mag,
              const uint16_t* __restrict__ k_low, const uint16_t* __restrict__ k_delta,
              int kv_heads, int64_t capacity, bool per_batch,
              const int64_t* __restrict__ head_to_kv, int64_t tokens,
              const int32_t* __restrict__ seq_len, float* __restrict__ scores, int64_t stride,
-             float scale, bool ref_div, uint32_t* __restrict__ score_hist, int hist_heads) {
+             float scale, bool ref_div, uint32_t* __restrict__ score_hist, int hist_heads,
+             int tile) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -102,8 +103,9 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
     const int kvh = blockIdx.y - b * kv_heads;
     int64_t L = seq_len ? static_cast<int64_t>(seq_len[b]) : tokens;
     L = L < tokens ? L : tokens;
-    const int64_t t_base = static_cast<int64_t>(blockIdx.x) * kTile;
+    const int64_t t_base = static_cast<int64_t>(blockIdx.x) * tile;  // tile <= kTile tokens
     if (t_base >= L) return;  // uniform over the CTA
+    const int64_t t_end = t_base + tile < L ? t_base + tile : L;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -114,7 +116,7 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
 #pragma unroll
     for (int j = 0; j < kTokensPerThread; ++j) {
         const int64_t t = t_base + j * kScoreThreads + tid;
-        if (t < L) rows[j].load(k_sign, k_mag, k_low, k_delta, (cache_head * capacity + t) * W);
+        if (t < t_end) rows[j].load(k_sign, k_mag, k_low, k_delta, (cache_head * capacity + t) * W);
     }
 
     // 2. Query heads of this KV head, in ascending head order.
@@ -206,7 +208,7 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
 #pragma unroll
         for (int j = 0; j < kTokensPerThread; ++j) {
             const int64_t t = t_base + j * kScoreThreads + tid;
-            if (t >= L) continue;
+            if (t >= t_end) continue;
             float score = 0.0f;
 #pragma unroll
             for (int w = 0; w < W; ++w) {
@@ -247,8 +249,18 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
                    int64_t cap, bool per_batch, const int64_t* h2k, int64_t tokens,
                    const int32_t* seq_len, float* scores, int64_t stride, float scale,
                    bool ref_div, bool vec, uint32_t* hist, cudaStream_t st) {
-    const dim3 grid((unsigned)((tokens + kTile - 1) / kTile), (unsigned)(batch * kv_heads));
-    const int hist_heads = hist ? (int)(q_heads < kHistHeads ? q_heads : kHistHeads) : 0;
+    // Tiles of at most kTile tokens, as many as keep two CTAs on every SM busy, so
+    // that no SM gets a larger share of the tokens than the others.
+    int64_t ntiles = (tokens + kTile - 1) / kTile;
+    const int64_t fill = (2 * num_sms()) / (batch * kv_heads);
+    if (fill > ntiles) ntiles = fill < tokens ? fill : tokens;
+    const int tile = (int)((tokens + ntiles - 1) / ntiles);
+    ntiles = (tokens + tile - 1) / tile;
+    const dim3 grid((unsigned)ntiles, (unsigned)(batch * kv_heads));
+    // Histogram rows in shared memory for the expected heads per KV head (a KV head
+    // with more skips the histogram; select then counts the top digit itself).
+    const int64_t per_kv = (q_heads + kv_heads - 1) / kv_heads;
+    const int hist_heads = hist ? (int)(per_kv < kHistHeads ? per_kv : kHistHeads) : 0;
     const size_t smem = (size_t)hist_heads * kBins * 4 + (size_t)(kScoreThreads / 32) * W * 32 * 4 +
                         (size_t)q_heads * (sizeof(int) + (size_t)W * 16);
     auto run = [&](auto kern) {
@@ -257,7 +269,7 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
         launch_pdl(kern, grid, dim3(kScoreThreads), smem, st,
 
             static_cast<const TQ*>(q), (int)q_heads, D, sg, mg, lo, de, (int)kv_heads, cap,
-            per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div, hist, hist_heads);
+            per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div, hist, hist_heads, tile);
     };
     if (vec) run(score_kernel<TQ, W, true>);
     else run(score_kernel<TQ, W, false>);

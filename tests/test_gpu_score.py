@@ -26,6 +26,30 @@ def test_score_bit_exact(qdtype, kvh, qh, tokens, dim):
     np.testing.assert_array_equal(got, ref)
 
 
+@pytest.mark.parametrize("kvh,qh,tokens,dim", [(4, 4, 2000, 128), (2, 6, 1500, 64), (8, 32, 2500, 128),
+                                               (2, 16, 1100, 128), (1, 12, 3000, 128), (2, 32, 700, 128),
+                                               (3, 12, 1024, 256), (2, 8, 4096, 96)])
+def test_score_aligned_capacity_head_groups_bit_exact(kvh, qh, tokens, dim):
+    """Bit-exact for 1 to 16 query heads per KV head and ragged last tiles; the
+    histograms add up to the row length (and are skipped above 8 heads per KV head)."""
+    k = synthetic_keys(kvh, tokens, dim, seed=tokens + dim, dtype=torch.bfloat16)
+    q = synthetic_keys(1, qh, dim, seed=tokens + 2, dtype=torch.bfloat16)
+    h2k = torch.arange(qh) // (qh // kvh)
+    cap = (tokens + 63) // 64 * 64
+    packed = pk.pack_keys(k.to(DEV), token_capacity=cap)
+    hist = pk.new_select_workspace(qh, tokens, DEV)
+    got = pk.score(q.to(DEV), packed, head_to_kv=h2k.to(DEV), tokens=tokens, hist=hist)
+    ref = O.score(q.float().numpy(), O.pack_keys(k.float().numpy(), capacity=cap),
+                  head_to_kv=h2k.numpy(), tokens=tokens)
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+    counts = hist[: qh * 2048 * 4].view(torch.int32).view(qh, 2048).sum(1).cpu()
+    per_kv = qh // kvh
+    if per_kv <= 8:
+        assert (counts == tokens).all()
+    else:  # histogram skipped for KV heads with more than 8 query heads
+        assert (counts == 0).all()
+
+
 def test_score_reference_tolerance(golden):
     """The reference test's own case (tests/test_popkv.py:45-54) against its readable scores."""
     keys, queries = golden["ref_test_shape/keys"], golden["ref_test_shape/queries"]
