@@ -784,35 +784,67 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     uint32_t prefix = sh.sel_bin << 21;
     remaining -= sh.sel_above;
 
-    // 3. Digits 2 (bits 20..10) and 3 (bits 9..0) over the keys left in the bin.
-    for (int j = 0; j < nvalid; ++j) {
-        const uint32_t x = mine[j];
-        if ((x >> 21) == (prefix >> 21)) atomicAdd(&sh.hist[1][hidx((x >> 10) & 0x7ffu)], 1u);
+    // 3. One sweep over this thread's keys sorts them by the top digit: above the
+    // threshold bin (certain picks, bitmap gt_bits) or in it (bitmap bin_bits,
+    // counted into the digit-2 histogram).  Bit j stands for token lo + first + j.
+    const uint32_t d1 = prefix >> 21;
+    uint32_t gt_w[2] = {0u, 0u}, bin_w[2] = {0u, 0u};  // bitmap halves: keys 0-31, 32-63
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int jn = nvalid - 32 * h < 32 ? nvalid - 32 * h : 32;
+        uint32_t g = 0u, bn = 0u;
+        for (int j = 0; j < jn; ++j) {
+            const uint32_t x = mine[32 * h + j];
+            const uint32_t top = x >> 21;
+            g |= static_cast<uint32_t>(top > d1) << j;
+            if (top == d1) {
+                bn |= 1u << j;
+                atomicAdd(&sh.hist[1][hidx((x >> 10) & 0x7ffu)], 1u);
+            }
+        }
+        gt_w[h] = g;
+        bin_w[h] = bn;
     }
+    uint64_t gt_bits = (static_cast<uint64_t>(gt_w[1]) << 32) | gt_w[0];
+    const uint64_t bin_bits = (static_cast<uint64_t>(bin_w[1]) << 32) | bin_w[0];
     cluster_find_bin<C>(sh, 1, kBins, remaining);
     // Every CTA of the cluster has now read the scorer's histogram: zero it for the next step.
     if (crank == 0)
         for (int i = tid; i < kBins; i += kRowThreads) hrow[i] = 0u;
-    prefix |= sh.sel_bin << 10;
+    const uint32_t d2 = sh.sel_bin;
+    prefix |= d2 << 10;
     remaining -= sh.sel_above;
     SEL_MARK(2);
-    for (int j = 0; j < nvalid; ++j) {
+    // Digit 3 over the keys of the digit-2 bin, visiting only the top-digit bin.
+    uint64_t bin2_bits = 0u;
+    for (uint64_t m = bin_bits; m != 0u; m &= m - 1) {
+        const int j = __ffsll(static_cast<long long>(m)) - 1;
         const uint32_t x = mine[j];
-        if ((x >> 10) == (prefix >> 10)) atomicAdd(&sh.hist[2][hidx(x & 0x3ffu)], 1u);
+        const uint32_t dx = (x >> 10) & 0x7ffu;
+        if (dx > d2) {
+            gt_bits |= 1ull << j;
+        } else if (dx == d2) {
+            bin2_bits |= 1ull << j;
+            atomicAdd(&sh.hist[2][hidx(x & 0x3ffu)], 1u);
+        }
     }
     cluster_find_bin<C>(sh, 2, 1024, remaining);
     const uint32_t thr = prefix | sh.sel_bin;
     const uint32_t need = remaining - sh.sel_above;
     SEL_MARK(3);
+    uint64_t eq_bits = 0u;
+    for (uint64_t m = bin2_bits; m != 0u; m &= m - 1) {
+        const int j = __ffsll(static_cast<long long>(m)) - 1;
+        const uint32_t x = mine[j];
+        if (x > thr) gt_bits |= 1ull << j;
+        else if (x == thr) eq_bits |= 1ull << j;
+    }
 
     // 4. Rank: (> thr) << 16 | (== thr) counts per thread (slice totals < 2^16), one
-    // exclusive block scan, the lower-ranked CTAs' totals, then each thread writes
-    // its picks in index order.
-    uint32_t cnt = 0u;
-    for (int j = 0; j < nvalid; ++j) {
-        const uint32_t x = mine[j];
-        cnt += x > thr ? 0x10000u : (x == thr ? 1u : 0u);
-    }
+    // exclusive block scan, the lower-ranked CTAs' totals, then the picks in index
+    // order: every key above thr and the first `need` keys equal to it.
+    const uint32_t cnt = (static_cast<uint32_t>(__popcll(gt_bits)) << 16) |
+                         static_cast<uint32_t>(__popcll(eq_bits));
     uint32_t incl = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -837,16 +869,15 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         cluster_arrive();
         cluster_wait();
         SEL_MARK(9);
-        if (tid == 0) {
+        if (warp == 0) {  // lane q < crank reads CTA q's totals; all loads in flight at once
             cg::cluster_group cluster = cg::this_cluster();
-            uint32_t g = 0u, e = 0u;
-            for (int q = 0; q < crank; ++q) {
-                const uint32_t t = cluster.map_shared_rank(&sh, q)->total;
-                g += t >> 16;
-                e += t & 0xffffu;
+            const uint32_t t = lane < crank ? cluster.map_shared_rank(&sh, lane)->total : 0u;
+            const uint32_t g = __reduce_add_sync(0xffffffffu, t >> 16);
+            const uint32_t e = __reduce_add_sync(0xffffffffu, t & 0xffffu);
+            if (lane == 0) {
+                sh.base_gt = g;
+                sh.base_eq = e;
             }
-            sh.base_gt = g;
-            sh.base_eq = e;
         }
         cluster_arrive();  // this CTA is done reading its peers
     } else if (tid == 0) {
@@ -854,19 +885,34 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         sh.base_eq = 0u;
     }
     __syncthreads();
+    SEL_MARK(10);
     const uint32_t before = incl - cnt + sh.wsum[warp];
+    // This CTA's picks take out[P0, P0 + n_c) (index order, the slice is contiguous):
+    // each thread writes its picks' token indices compacted into shared memory (over
+    // the keys, no longer needed), and the CTA stores them coalesced.
+    const uint32_t need_left = need;
+    const uint32_t eq_c = sh.total & 0xffffu, gt_c = sh.total >> 16;
+    const uint32_t p0 = sh.base_gt + min(sh.base_eq, need_left);
+    const uint32_t n_c = gt_c + min(sh.base_eq + eq_c, need_left) - min(sh.base_eq, need_left);
     uint32_t gb = sh.base_gt + (before >> 16), eb = sh.base_eq + (before & 0xffffu);
-    if (cnt != 0u) {
-        for (int j = 0; j < nvalid; ++j) {
-            const uint32_t x = mine[j];
-            if (x > thr || (x == thr && eb < need)) {
-                const int32_t t = static_cast<int32_t>(lo + first + j);
-                if (r.out) r.out[gb + min(eb, need)] = t;
-                if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
-            }
-            gb += x > thr;
-            eb += x == thr;
-        }
+    const uint32_t p_start = gb + min(eb, need_left) - p0;
+    uint64_t picks = gt_bits;
+    for (uint64_t m = eq_bits; m != 0u && eb < need_left; m &= m - 1, ++eb)
+        picks |= m & (~m + 1);  // lowest remaining tie
+    // (every key was read before the scan's barriers: s_keys may be overwritten)
+    int32_t* s_out = reinterpret_cast<int32_t*>(s_keys);
+    uint32_t pos = p_start;
+    while (picks != 0u) {
+        const int j = __ffsll(static_cast<long long>(picks)) - 1;
+        picks &= picks - 1;
+        s_out[pos++] = static_cast<int32_t>(lo + first + j);
+    }
+    __syncthreads();
+    SEL_MARK(13);
+    for (uint32_t i = tid; i < n_c; i += kRowThreads) {
+        const int32_t t = s_out[i];
+        if (r.out) r.out[p0 + i] = t;
+        if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
     }
     SEL_MARK(4);
     if constexpr (C > 1) cluster_wait();  // peers are done reading this CTA's shared memory
