@@ -91,8 +91,8 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
     pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint32_t* s_hist = reinterpret_cast<uint32_t*>(smem_raw);         // [hist_heads][kBins]
-    float* s_abs = reinterpret_cast<float*>(s_hist + hist_heads * kBins);  // [warps][W*32]
-    int* s_heads = reinterpret_cast<int*>(s_abs + (kScoreThreads / 32) * W * 32);  // [q_heads]
+    float* s_abs = reinterpret_cast<float*>(s_hist + hist_heads * kBins);  // [warps][W*33]
+    int* s_heads = reinterpret_cast<int*>(s_abs + (kScoreThreads / 32) * W * 33);  // [q_heads]
     uint32_t* s_qs = reinterpret_cast<uint32_t*>(s_heads + q_heads);  // [q_heads][W]
     uint32_t* s_qm = s_qs + q_heads * W;
     float* s_ql = reinterpret_cast<float*>(s_qm + q_heads * W);
@@ -139,7 +139,7 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
     // words; lane j then sums word j's magnitudes in channel order from shared memory.
     if (use_hist)
         for (int i = tid; i < nh * kBins; i += kScoreThreads) s_hist[i] = 0u;
-    float* my_abs = s_abs + warp * (W * 32);
+    float* my_abs = s_abs + warp * (W * 33);  // word j at 33 j: conflict-free column reads
     for (int slot = warp; slot < nh; slot += kScoreThreads / 32) {
         const TQ* q = queries + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * D;
         float v[W];
@@ -149,7 +149,7 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
             const int c = 32 * j + lane;
             v[j] = c < D ? to_float<TQ>(q[c]) : 0.0f;
             if (c < D) { mn = fminf(mn, v[j]); mx = fmaxf(mx, v[j]); }
-            my_abs[32 * j + lane] = fabsf(v[j]);
+            my_abs[33 * j + lane] = fabsf(v[j]);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -169,14 +169,19 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
         }
         __syncwarp();
         if (lane < W) {
+            // Channel-order sums without branches: each magnitude goes to both sums, as
+            // itself or as +0 (which leaves a sum of magnitudes unchanged); channels past
+            // D hold 0.
             float ls = 0.0f, hs = 0.0f;
-            int lc = 0, hc = 0;
             const int n = min(32, D - 32 * lane);
-            for (int i = 0; i < n; ++i) {
-                const float x = my_abs[32 * lane + i];
-                if ((my_mw >> i) & 1u) { hs += x; ++hc; }
-                else { ls += x; ++lc; }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float x = my_abs[33 * lane + i];
+                const bool high = (my_mw >> i) & 1u;
+                hs += high ? x : 0.0f;
+                ls += high ? 0.0f : x;
             }
+            const int hc = __popc(my_mw), lc = n - hc;
             float low, high;
             representatives(ls, lc, hs, hc, ref_div, low, high);
             s_qs[slot * W + lane] = my_sw;
@@ -261,7 +266,7 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
     // with more skips the histogram; select then counts the top digit itself).
     const int64_t per_kv = (q_heads + kv_heads - 1) / kv_heads;
     const int hist_heads = hist ? (int)(per_kv < kHistHeads ? per_kv : kHistHeads) : 0;
-    const size_t smem = (size_t)hist_heads * kBins * 4 + (size_t)(kScoreThreads / 32) * W * 32 * 4 +
+    const size_t smem = (size_t)hist_heads * kBins * 4 + (size_t)(kScoreThreads / 32) * W * 33 * 4 +
                         (size_t)q_heads * (sizeof(int) + (size_t)W * 16);
     auto run = [&](auto kern) {
         if (smem > 48 * 1024)
