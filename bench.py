@@ -353,6 +353,7 @@ def run_ours(args):
     h2d = host_q[0].nbytes + host_k[0].nbytes + host_v[0].nbytes
     d2h = host_out.nbytes
 
+    peer_errors = stack.peer_errors() if world > 1 else 0
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_ms, cores = time_cpu_reference(L0, budget, args.cpu_sample_steps, 1)
@@ -370,7 +371,9 @@ def run_ours(args):
             "config": {"workload": "configs[1]: Llama-3.1-8B attention layer, 32 q / 8 kv heads, "
                                    "head_dim 128, bf16 cache, group 32, one append per step",
                        "context": L0, "budget": budget, "layers_per_step": layers,
-                       "sequences": B, "parallelism": f"kv-head shards x{world}" if world > 1 else "none",
+                       "sequences": B, "parallelism": (f"kv-head shards x{world}, " + ("output all-gather fused into the attention combine (NVLink peer stores)"
+                                                                       if stack.peer is not None else "NCCL all-gather per layer"))
+                                      if world > 1 else "none",
                        "l2": "inputs larger than L2 (32 layers rotate through ~4.7 GB per GPU)",
                        "graph": "one CUDA graph per decode step"},
             "hbm_gbs_step": step_bytes / (ms_layer * 1e-3) / 1e9,
@@ -385,6 +388,8 @@ def run_ours(args):
             "gpu_launches": stack.launches_per_step() * args.steps,
             "cpu_baseline": cpu_baseline,
         }
+        if world > 1 and peer_errors:
+            line["error"] = f"{peer_errors} peer all-gather waits ran out"
         print(json.dumps(line), flush=True)
     if world > 1:
         # Tearing NCCL down while captured graphs still reference its communicator can

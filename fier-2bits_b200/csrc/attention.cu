@@ -34,6 +34,7 @@ constexpr int kMaxGroup = 16;
 constexpr int kSegMax = 2048;   // tokens per segment (multiple of 8)
 constexpr int kTileRows = 16;
 constexpr int kMaxSplits = 1024;
+constexpr int kMaxPeers = 8;       // ranks of one NVLink domain in a peer all-gather
 
 // Phase timestamps for tuning builds (-DPOPKV_ATTN_PROFILE): thread 0 of each CTA
 // records globaltimer at phase boundaries (8 slots per CTA).
@@ -75,6 +76,13 @@ struct AttnParams {
     float sl2;       // 1/sqrt(D) * log2(e)
     int work_bytes;  // scratch bytes before the token list (SIMT kernel)
     int dense;       // attend every token 0..L (no head masks)
+    // Peer all-gather of the output (world > 1): row r of this rank's out also goes
+    // to row rank * B * QH + r of every rank's gathered buffer, then the ranks
+    // exchange arrival flags (see combine_kernel).
+    int world, rank;
+    void* peer_out[kMaxPeers];        // gathered buffer base on each rank
+    uint32_t* peer_flags[kMaxPeers];  // each rank's [world] arrival words of this layer
+    uint32_t* sync;                   // this rank's [3]: CTA ticket, epoch, error
 };
 
 __device__ __forceinline__ int64_t seq_length(const AttnParams& p, int b) {
@@ -180,6 +188,66 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
     return total;
 }
 
+// ------------------------------------------------------- peer all-gather
+// The combine of a rank writes each output row straight into every rank's gathered
+// buffer over NVLink (plain stores to peer memory), so no separate collective runs.
+// Completion: every CTA makes its stores visible system-wide and takes a ticket; the
+// last CTA bumps this layer's epoch, stores it (release, system scope) into its slot
+// of every rank's arrival words, and waits until every rank's word for this layer
+// reaches the epoch (acquire) -- the gathered buffer is then complete here when the
+// kernel ends, as after an all-gather.  The wait is bounded (~2 s); running out of it
+// sets the error word and returns.  Epochs only grow, so no flag is ever reset, and a
+// rank cannot overwrite a row before its peers have passed the layer that reads it.
+constexpr long long kPeerWaitNs = 2000000000ll;
+
+__device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+template <int DPT, typename T>
+__device__ void peer_gather_rows(const AttnParams& p, int64_t row, const float (&o)[DPT], float inv) {
+    const int64_t dst_row = static_cast<int64_t>(p.rank) * p.B * p.QH + row;
+    for (int j = 0; j < p.world; ++j) {
+        T* dst = static_cast<T*>(p.peer_out[j]) + dst_row * p.D;
+#pragma unroll
+        for (int c = 0; c < DPT; ++c) {
+            const int d = threadIdx.x + 128 * c;
+            if (d < p.D) dst[d] = from_float<T>(o[c] * inv);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const uint32_t t = atomicAdd(p.sync, 1u);
+    if (t != gridDim.x - 1) return;
+    __threadfence_system();  // the other CTAs' stores, seen through their tickets, come first
+    p.sync[0] = 0u;           // every CTA has taken its ticket: ready for the next call
+    const uint32_t epoch = p.sync[1] + 1u;
+    p.sync[1] = epoch;
+    for (int j = 0; j < p.world; ++j) store_release_sys(p.peer_flags[j] + p.rank, epoch);
+    const uint32_t* mine = p.peer_flags[p.rank];
+    const unsigned long long t0 = global_ns();
+    for (int j = 0; j < p.world; ++j) {
+        while (static_cast<int32_t>(load_acquire_sys(mine + j) - epoch) < 0) {
+            if (global_ns() - t0 > static_cast<unsigned long long>(kPeerWaitNs)) {
+                atomicExch(p.sync + 2, 1u);
+                return;
+            }
+            __nanosleep(256);
+        }
+    }
+}
+
 // ----------------------------------------------------------------- combine
 // One CTA per (sequence, query head): merges the S segment partials (max, sum,
 // acc) into the output.  Every warp walks the splits in chunks of 32 with an online
@@ -255,6 +323,7 @@ __global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
         const int d = tid + 128 * c;
         if (d < D) out[row * D + d] = from_float<T>(o[c] * inv);
     }
+    if (p.world > 1) peer_gather_rows<DPT, T>(p, row, o, inv);
     COMB_MARK(1);
 }
 
@@ -803,7 +872,8 @@ static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t
                           const int32_t* indices, int64_t index_stride, int64_t budget,
                           int64_t tokens, const int32_t* seq_len, void* out, void* workspace,
                           size_t workspace_bytes, int64_t splits, popkv_stream_t stream,
-                          int mode) {
+                          int mode, int world = 1, int rank = 0, void* const* peer_out = nullptr,
+                          uint32_t* const* peer_flags = nullptr, uint32_t* sync_words = nullptr) {
     const size_t es = dtype_size(dtype);
     if (es == 0) return fail(POPKV_ERR_UNSUPPORTED, "dtype %d is not fp32/fp16/bf16", dtype);
     if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0)
@@ -851,6 +921,24 @@ static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t
     p.sl2 = (float)((1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634);
     p.work_bytes = 0;
     p.dense = mode == kDense;
+    p.world = 1;
+    p.rank = 0;
+    p.sync = nullptr;
+    for (int j = 0; j < kMaxPeers; ++j) { p.peer_out[j] = nullptr; p.peer_flags[j] = nullptr; }
+    if (world > 1) {
+        if (world > kMaxPeers || rank < 0 || rank >= world || !peer_out || !peer_flags || !sync_words)
+            return fail(POPKV_ERR_INVALID_ARGUMENT, "peer gather needs 1 < world <= %d, rank < world, peer "
+                        "pointers and sync words", kMaxPeers);
+        for (int j = 0; j < world; ++j) {
+            if (!peer_out[j] || !peer_flags[j] || !aligned(peer_out[j], 16) || !aligned(peer_flags[j], 4))
+                return fail(POPKV_ERR_INVALID_ARGUMENT, "peer %d: null or misaligned gather pointer", j);
+            p.peer_out[j] = peer_out[j];
+            p.peer_flags[j] = peer_flags[j];
+        }
+        p.world = world;
+        p.rank = rank;
+        p.sync = sync_words;
+    }
     const cudaStream_t st = as_stream(stream);
 
     if (mode == kFromIndices) {
@@ -900,6 +988,19 @@ extern "C" int popkv_sparse_attention_premasked(
                           kv_heads, kv_capacity, cache_per_batch, current_keys, current_values,
                           nullptr, 0, 2, tokens, seq_len, out, workspace, workspace_bytes, splits,
                           stream, kPremasked);
+}
+
+extern "C" int popkv_sparse_attention_premasked_gather(
+    const void* queries, int dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* key_cache, const void* value_cache, int64_t kv_heads, int64_t kv_capacity,
+    int cache_per_batch, const void* current_keys, const void* current_values, int64_t tokens,
+    const int32_t* seq_len, void* out, void* workspace, size_t workspace_bytes, int64_t splits,
+    int world, int rank, void* const* peer_out, uint32_t* const* peer_flags, uint32_t* sync_words,
+    popkv_stream_t stream) {
+    return attention_impl(queries, dtype, batch, q_heads, head_dim, key_cache, value_cache,
+                          kv_heads, kv_capacity, cache_per_batch, current_keys, current_values,
+                          nullptr, 0, 2, tokens, seq_len, out, workspace, workspace_bytes, splits,
+                          stream, kPremasked, world, rank, peer_out, peer_flags, sync_words);
 }
 
 extern "C" int popkv_sparse_attention_masks(void* workspace, int64_t batch, int64_t q_heads,

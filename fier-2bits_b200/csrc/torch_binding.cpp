@@ -330,7 +330,9 @@ at::Tensor sparse_attention_premasked(const at::Tensor& queries, const at::Tenso
                                      const at::Tensor& value_cache, int64_t tokens,
                                      const at::Tensor& current_keys, const at::Tensor& current_values,
                                      const c10::optional<at::Tensor>& seq_len,
-                                     const at::Tensor& workspace, int64_t splits, const at::Tensor& out) {
+                                     const at::Tensor& workspace, int64_t splits, const at::Tensor& out,
+                                     std::vector<int64_t> peer_out, std::vector<int64_t> peer_flags,
+                                     int64_t rank, const c10::optional<at::Tensor>& sync_words) {
     for (const at::Tensor* t : {&queries, &key_cache, &value_cache, &current_keys, &current_values, &workspace, &out}) {
         CHECK_CUDA(*t); CHECK_CONTIGUOUS(*t);
     }
@@ -341,11 +343,30 @@ at::Tensor sparse_attention_premasked(const at::Tensor& queries, const at::Tenso
     const int32_t* sl = nullptr;
     if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
     c10::cuda::CUDAGuard guard(queries.device());
-    const int rc = popkv_sparse_attention_premasked(
-        queries.data_ptr(), dtype_code(queries), batch, q_heads, dim, key_cache.data_ptr(),
-        value_cache.data_ptr(), kv_heads, key_cache.size(2), 1, current_keys.data_ptr(),
-        current_values.data_ptr(), tokens, sl, out.data_ptr(), workspace.data_ptr(),
-        (size_t)workspace.nbytes(), splits, stream_of(queries));
+    int rc;
+    if (peer_out.empty()) {
+        rc = popkv_sparse_attention_premasked(
+            queries.data_ptr(), dtype_code(queries), batch, q_heads, dim, key_cache.data_ptr(),
+            value_cache.data_ptr(), kv_heads, key_cache.size(2), 1, current_keys.data_ptr(),
+            current_values.data_ptr(), tokens, sl, out.data_ptr(), workspace.data_ptr(),
+            (size_t)workspace.nbytes(), splits, stream_of(queries));
+    } else {
+        // Peer all-gather: device addresses of every rank's gathered buffer and arrival
+        // words (mapped into this process), this rank's sync words.
+        TORCH_CHECK(sync_words && peer_flags.size() == peer_out.size(), "peer gather needs flags and sync words");
+        CHECK_CUDA(*sync_words); CHECK_DTYPE(*sync_words, at::kInt);
+        TORCH_CHECK(sync_words->numel() >= 3, "sync words hold 3 entries");
+        std::vector<void*> outs;
+        std::vector<uint32_t*> flags;
+        for (int64_t a : peer_out) outs.push_back(reinterpret_cast<void*>(a));
+        for (int64_t a : peer_flags) flags.push_back(reinterpret_cast<uint32_t*>(a));
+        rc = popkv_sparse_attention_premasked_gather(
+            queries.data_ptr(), dtype_code(queries), batch, q_heads, dim, key_cache.data_ptr(),
+            value_cache.data_ptr(), kv_heads, key_cache.size(2), 1, current_keys.data_ptr(),
+            current_values.data_ptr(), tokens, sl, out.data_ptr(), workspace.data_ptr(),
+            (size_t)workspace.nbytes(), splits, (int)outs.size(), (int)rank, outs.data(), flags.data(),
+            reinterpret_cast<uint32_t*>(sync_words->data_ptr<int32_t>()), stream_of(queries));
+    }
     check_status(rc, "popkv_sparse_attention_premasked");
     return out;
 }
@@ -377,7 +398,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("seq_len") = py::none(), py::arg("rows_per_seq") = 0, py::arg("out") = py::none(),
           py::arg("attn_workspace") = py::none(), py::arg("attn_sizes") = std::vector<int64_t>{},
           py::arg("hist") = py::none());
-    m.def("sparse_attention_premasked", &sparse_attention_premasked);
+    m.def("sparse_attention_premasked", &sparse_attention_premasked, py::arg("queries"), py::arg("key_cache"),
+          py::arg("value_cache"), py::arg("tokens"), py::arg("current_keys"), py::arg("current_values"),
+          py::arg("seq_len"), py::arg("workspace"), py::arg("splits"), py::arg("out"),
+          py::arg("peer_out") = std::vector<int64_t>{}, py::arg("peer_flags") = std::vector<int64_t>{},
+          py::arg("rank") = 0, py::arg("sync_words") = py::none());
     m.def("sparse_attention", &sparse_attention, py::arg("queries"), py::arg("key_cache"),
           py::arg("value_cache"), py::arg("indices"), py::arg("budget"), py::arg("tokens"),
           py::arg("current_keys") = py::none(), py::arg("current_values") = py::none(),

@@ -168,7 +168,9 @@ class RetrievalStack:
 
     With ``process_group`` (NCCL) of size W the stack holds KV heads
     [r*KVH/W, (r+1)*KVH/W) of every sequence and all-gathers each layer's
-    attention output over the group.
+    attention output over the group: with POPKV_GATHER=peer inside the attention's
+    combine kernel over NVLink peer memory, otherwise by an NCCL all-gather after it
+    (``gathered`` either way).
     """
 
     def __init__(self, *, layers: int, batch: int, kv_heads: int, q_heads: int, head_dim: int,
@@ -212,8 +214,18 @@ class RetrievalStack:
         self.k_in = torch.zeros(layers, B, H, head_dim, dtype=dtype, device=dev)
         self.v_in = torch.zeros(layers, B, H, head_dim, dtype=dtype, device=dev)
         self.out = torch.zeros(layers, B, QH, head_dim, dtype=dtype, device=dev)
-        self.gathered = (torch.zeros(layers, self.world * B, QH, head_dim, dtype=dtype, device=dev)
-                         if self.world > 1 else None)
+        # world > 1: an NCCL all-gather after the attention, or with POPKV_GATHER=peer
+        # the attention combine all-gathers each layer's output over NVLink peer
+        # memory (symmetric buffers).
+        self.peer = None
+        self.gathered = None
+        if self.world > 1:
+            import os
+            if os.environ.get("POPKV_GATHER", "nccl") == "nccl":
+                self.gathered = torch.zeros(layers, self.world * B, QH, head_dim, dtype=dtype, device=dev)
+            else:
+                self.peer = pk.PeerGather(layers, B * QH, head_dim, dtype, group=process_group)
+                self.gathered = self.peer.gathered.view(layers, self.world * B, QH, head_dim)
         self.graph = None
         # The append of a layer only has to follow that layer's score, so it runs on a
         # side stream in parallel with select and attention; steps join it at the end.
@@ -252,8 +264,9 @@ class RetrievalStack:
         pk.sparse_attention_premasked(self.q_in[i], self.key_cache[i], self.value_cache[i],
                                       tokens=tokens, current_keys=self.k_in[i],
                                       current_values=self.v_in[i], seq_len=self.seq_len,
-                                      workspace=self.workspace[i], out=self.out[i])
-        if self.world > 1:
+                                      workspace=self.workspace[i], out=self.out[i],
+                                      gather=self.peer, layer=i)
+        if self.world > 1 and self.peer is None:
             import torch.distributed as dist
             dist.all_gather_into_tensor(self.gathered[i], self.out[i], group=self.group)
 
@@ -290,6 +303,10 @@ class RetrievalStack:
         torch.cuda.current_stream().wait_stream(stream)
         # Capturing enqueued nothing: the graph is replayed by step().
         self.graph = g
+
+    def peer_errors(self) -> int:
+        """Peer all-gather waits that ran out (0 on a healthy run)."""
+        return 0 if self.peer is None else self.peer.errors()
 
     def launches_per_step(self) -> int:
         # score, select, attention + combine, append per layer, + advance.

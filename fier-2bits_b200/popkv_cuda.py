@@ -108,14 +108,67 @@ def select(scores: torch.Tensor, *, budget: int, tokens: int | None = None,
 
 
 def sparse_attention_premasked(queries, key_cache, value_cache, *, tokens: int, current_keys,
-                               current_values, workspace, out, seq_len=None, splits: int = 0):
+                               current_values, workspace, out, seq_len=None, splits: int = 0,
+                               gather: "PeerGather | None" = None, layer: int = 0):
     """sparse_attention over the bitmask that ``select(attn_workspace=workspace)`` wrote.
 
     Batched caches [B, KVH, kv_cap, D]; queries/out [B, QH, D]; current rows [B, KVH, D].
+    With ``gather`` (a :class:`PeerGather` of this rank), the output rows are also
+    all-gathered over NVLink peer memory into ``gather.gathered[layer]`` of every rank.
     """
+    if gather is None:
+        return extension().sparse_attention_premasked(queries, key_cache, value_cache, int(tokens),
+                                                      current_keys, current_values, seq_len,
+                                                      workspace, int(splits), out)
     return extension().sparse_attention_premasked(queries, key_cache, value_cache, int(tokens),
                                                   current_keys, current_values, seq_len,
-                                                  workspace, int(splits), out)
+                                                  workspace, int(splits), out,
+                                                  gather.out_ptrs(layer), gather.flag_ptrs(layer),
+                                                  gather.rank, gather.sync[layer])
+
+
+class PeerGather:
+    """Buffers of the fused peer all-gather (one process per GPU, one NVLink domain).
+
+    ``gathered`` [layers, world * rows, head_dim] and the arrival words [layers, world]
+    live in symmetric memory (every rank maps every rank's copy); ``sync`` [layers, 3]
+    holds this rank's ticket / epoch / error words.  Built collectively by all ranks.
+    """
+
+    def __init__(self, layers: int, rows: int, head_dim: int, dtype, group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer all-gather spans at most 8 ranks")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.rows, self.head_dim = int(rows), int(head_dim)
+        self.gathered = symm_mem.empty(layers, self.world * rows, head_dim, dtype=dtype, device=dev)
+        self.flags = symm_mem.empty(layers, self.world, dtype=torch.int32, device=dev)
+        self.flags.zero_()
+        self.gathered.zero_()
+        torch.cuda.synchronize()
+        group_name = group.group_name if group is not None else dist.group.WORLD.group_name
+        self._hg = symm_mem.rendezvous(self.gathered, group_name)
+        self._hf = symm_mem.rendezvous(self.flags, group_name)
+        self.sync = torch.zeros(layers, 3, dtype=torch.int32, device=dev)
+        self._out_stride = self.world * rows * head_dim * self.gathered.element_size()
+        self._flag_stride = self.world * 4
+
+    @staticmethod
+    def _peer_bases(handle, tensor, rank) -> list:
+        off = tensor.data_ptr() - int(handle.buffer_ptrs[rank])  # the tensor's place in its buffer
+        return [int(p) + off for p in handle.buffer_ptrs]
+
+    def out_ptrs(self, layer: int) -> list:
+        return [p + layer * self._out_stride for p in self._peer_bases(self._hg, self.gathered, self.rank)]
+
+    def flag_ptrs(self, layer: int) -> list:
+        return [p + layer * self._flag_stride for p in self._peer_bases(self._hf, self.flags, self.rank)]
+
+    def errors(self) -> int:
+        return int(self.sync[:, 2].sum().item())
 
 
 def sparse_attention(queries: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,

@@ -186,6 +186,27 @@ int popkv_sparse_attention_premasked(const void* queries, int dtype, int64_t bat
                                      int64_t tokens, const int32_t* seq_len, void* out,
                                      void* workspace, size_t workspace_bytes, int64_t splits,
                                      popkv_stream_t stream);
+/*
+ * popkv_sparse_attention_premasked whose output rows are also all-gathered over
+ * NVLink peer memory, in place of a separate collective after it (the reference
+ * runs one GPU and has no counterpart; this serves the KV-head-sharded decode).
+ * Rank `rank` of `world` (<= 8, one process per GPU) writes its out row r into row
+ * rank * batch * q_heads + r of every rank's gathered buffer (peer_out[j]: rank j's
+ * buffer, [world * batch * q_heads, head_dim], mapped into this process), then
+ * stores this layer's epoch into word `rank` of every rank's arrival words
+ * (peer_flags[j]: rank j's [world] uint32, zero-initialised once) and waits until
+ * all `world` of its own words hold the epoch: on return of the stream work the
+ * gathered buffer is complete on this rank.  sync_words: this rank's [3] uint32
+ * (zeroed once): CTA ticket, epoch, error (1 after a wait ran out, ~2 s).  Every rank
+ * must make the same sequence of calls for a given set of buffers.
+ */
+int popkv_sparse_attention_premasked_gather(
+    const void* queries, int dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
+    const void* key_cache, const void* value_cache, int64_t kv_heads, int64_t kv_capacity,
+    int cache_per_batch, const void* current_keys, const void* current_values, int64_t tokens,
+    const int32_t* seq_len, void* out, void* workspace, size_t workspace_bytes, int64_t splits,
+    int world, int rank, void* const* peer_out, uint32_t* const* peer_flags, uint32_t* sync_words,
+    popkv_stream_t stream);
 /* Token-bitmask region of an attention workspace (for popkv_select's head_masks). */
 int popkv_sparse_attention_masks(void* workspace, int64_t batch, int64_t q_heads,
                                  int64_t kv_heads, int64_t head_dim, int64_t tokens,
