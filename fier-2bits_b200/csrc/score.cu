@@ -7,14 +7,14 @@
 //   fmaf(ql*kl, Cs, fmaf(dq*kl, Cq, fmaf(ql*dk, Ck, dq*dk*Cqk)))
 // with Cs/Cq/Ck/Cqk = 2*popc(match & x) - popc(x), then multiplied by 1/sqrt(D).
 //
-// B200 layout of the work: one CTA per (sequence, KV head, 512-token tile) serves
-// every query head mapped to that KV head, so each packed row (48 B at D = 128)
-// is read from HBM once for the whole GQA group (the reference re-reads it once
-// per query head).  Each thread owns two tokens and fetches their sign/mag words
-// with 16-byte loads and low/delta with 8-byte loads, issued before the query
-// pack so that the HBM latency overlaps it.  The query pack itself is
-// warp-parallel (ballots for the bit words) with the sequential channel-order
-// sums kept on one lane per word.
+// B200 layout of the work: one CTA per (sequence, KV head, token tile of at most
+// 1024 tokens, sized so that every SM holds two CTAs) serves every query head
+// mapped to that KV head, so each packed row (48 B at D = 128) is read from HBM once
+// for the whole GQA group (the reference re-reads it once per query head).  Each
+// thread owns four tokens and fetches their sign/mag words with 16-byte loads and
+// low/delta with 8-byte loads, issued before the query pack so that the HBM latency
+// overlaps it.  The query pack is warp-parallel (ballots for the bit words) with the
+// sequential channel-order sums kept on one lane per word.
 #include <cmath>
 
 #include "common.cuh"
@@ -195,6 +195,20 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
 
     const uint32_t last_valid = (D & 31) ? ((1u << (D & 31)) - 1u) : 0xffffffffu;
     const float sc = ref_div ? rsqrtf(static_cast<float>(D)) : scale;
+    // popc of each token's magnitude words does not depend on the query head: counted
+    // once per token (one byte per word, W <= 4) instead of once per head.
+    uint32_t pkm[kTokensPerThread];
+#pragma unroll
+    for (int j = 0; j < kTokensPerThread; ++j) {
+        pkm[j] = 0u;
+        if constexpr (W <= 4) {
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
+                pkm[j] |= static_cast<uint32_t>(__popc(rows[j].m[w] & valid)) << (8 * w);
+            }
+        }
+    }
     for (int slot = 0; slot < nh; ++slot) {
         float* out = scores + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * stride;
         uint32_t* hist = s_hist + slot * kBins;
@@ -223,7 +237,8 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
                 const uint32_t both = qm[w] & km;
                 const int cs = 2 * __popc(match) - __popc(valid);
                 const int cq = 2 * __popc(match & qm[w]) - pq[w];
-                const int ck = 2 * __popc(match & km) - __popc(km);
+                const int pk = W <= 4 ? static_cast<int>((pkm[j] >> (8 * w)) & 0xffu) : __popc(km);
+                const int ck = 2 * __popc(match & km) - pk;
                 const int cqk = 2 * __popc(match & both) - __popc(both);
                 const float kl = __half2float(__ushort_as_half(rows[j].l[w]));
                 const float dk = __half2float(__ushort_as_half(rows[j].d[w]));
