@@ -168,8 +168,8 @@ class RetrievalStack:
 
     With ``process_group`` (NCCL) of size W the stack holds KV heads
     [r*KVH/W, (r+1)*KVH/W) of every sequence and all-gathers each layer's
-    attention output over the group: with POPKV_GATHER=peer inside the attention's
-    combine kernel over NVLink peer memory, otherwise by an NCCL all-gather after it
+    attention output over the group: inside the attention's combine kernel over
+    NVLink peer memory, or with POPKV_GATHER=nccl by an NCCL all-gather after it
     (``gathered`` either way).
     """
 
@@ -214,14 +214,14 @@ class RetrievalStack:
         self.k_in = torch.zeros(layers, B, H, head_dim, dtype=dtype, device=dev)
         self.v_in = torch.zeros(layers, B, H, head_dim, dtype=dtype, device=dev)
         self.out = torch.zeros(layers, B, QH, head_dim, dtype=dtype, device=dev)
-        # world > 1: an NCCL all-gather after the attention, or with POPKV_GATHER=peer
-        # the attention combine all-gathers each layer's output over NVLink peer
-        # memory (symmetric buffers).
+        # world > 1: the attention combine all-gathers each layer's output over NVLink
+        # peer memory (symmetric buffers); POPKV_GATHER=nccl selects an NCCL
+        # all-gather after the attention instead.
         self.peer = None
         self.gathered = None
         if self.world > 1:
             import os
-            if os.environ.get("POPKV_GATHER", "nccl") == "nccl":
+            if os.environ.get("POPKV_GATHER", "peer") == "nccl":
                 self.gathered = torch.zeros(layers, self.world * B, QH, head_dim, dtype=dtype, device=dev)
             else:
                 self.peer = pk.PeerGather(layers, B * QH, head_dim, dtype, group=process_group)
