@@ -229,6 +229,16 @@ def run_ours(args):
     clocks.stop()
     barrier()
     elapsed = torch.tensor([start.elapsed_time(end)], device=dev)
+    gather_check = None
+    if world > 1:
+        # The last timed step's all-gathered outputs against an NCCL all-gather of
+        # every rank's own outputs of that step: bit for bit.
+        ref = torch.empty_like(stack.gathered)
+        for i in range(layers):
+            dist.all_gather_into_tensor(ref[i], stack.out[i], group=group)
+        bad = torch.tensor([int((ref != stack.gathered).any(dim=-1).sum())], device=dev)
+        dist.all_reduce(bad)
+        gather_check = "ok" if int(bad) == 0 else f"{int(bad)} rows differ"
     if world > 1:
         dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
     ms_step = float(elapsed) / args.steps
@@ -388,6 +398,9 @@ def run_ours(args):
             "gpu_launches": stack.launches_per_step() * args.steps,
             "cpu_baseline": cpu_baseline,
         }
+        if world > 1:
+            line["gather_check"] = gather_check
+            line["config"]["gather_wait"] = stack.gather_wait if stack.peer is not None else "nccl"
         if world > 1 and peer_errors:
             line["error"] = f"{peer_errors} peer all-gather waits ran out"
         print(json.dumps(line), flush=True)

@@ -36,21 +36,6 @@ constexpr int kTileRows = 16;
 constexpr int kMaxSplits = 1024;
 constexpr int kMaxPeers = 8;       // ranks of one NVLink domain in a peer all-gather
 
-// Phase timestamps for tuning builds (-DPOPKV_ATTN_PROFILE): thread 0 of each CTA
-// records globaltimer at phase boundaries (8 slots per CTA).
-#ifdef POPKV_ATTN_PROFILE
-__device__ unsigned long long g_attn_marks[65536 * 8];
-#define ATTN_MARK(i) do { if (threadIdx.x == 0) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_attn_marks[(blockIdx.y * gridDim.x + blockIdx.x) * 8 + (i)] = t; } } while (0)
-#else
-#define ATTN_MARK(i) do { } while (0)
-#endif
-#ifdef POPKV_ATTN_PROFILE
-__device__ unsigned long long g_comb_marks[65536 * 2];
-#define COMB_MARK(i) do { if (threadIdx.x == 0) { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); g_comb_marks[blockIdx.x * 2 + (i)] = t; } } while (0)
-#else
-#define COMB_MARK(i) do { } while (0)
-#endif
-
 struct AttnParams {
     const void* q;
     const void* kc;
@@ -83,6 +68,7 @@ struct AttnParams {
     void* peer_out[kMaxPeers];        // gathered buffer base on each rank
     uint32_t* peer_flags[kMaxPeers];  // each rank's [world] arrival words of this layer
     uint32_t* sync;                   // this rank's [3]: CTA ticket, epoch, error
+    int peer_defer;                   // publish arrival only; popkv_peer_gather_wait waits
 };
 
 __device__ __forceinline__ int64_t seq_length(const AttnParams& p, int b) {
@@ -190,14 +176,20 @@ __device__ int build_union(const AttnParams& p, int b, int kvh, int64_t lo, int 
 
 // ------------------------------------------------------- peer all-gather
 // The combine of a rank writes each output row straight into every rank's gathered
-// buffer over NVLink (plain stores to peer memory), so no separate collective runs.
+// buffer over NVLink (16-byte stores to peer memory), so no separate collective runs.
 // Completion: every CTA makes its stores visible system-wide and takes a ticket; the
-// last CTA bumps this layer's epoch, stores it (release, system scope) into its slot
-// of every rank's arrival words, and waits until every rank's word for this layer
-// reaches the epoch (acquire) -- the gathered buffer is then complete here when the
-// kernel ends, as after an all-gather.  The wait is bounded (~2 s); running out of it
-// sets the error word and returns.  Epochs only grow, so no flag is ever reset, and a
-// rank cannot overwrite a row before its peers have passed the layer that reads it.
+// last CTA bumps this layer's epoch and stores it (release, system scope) into its
+// slot of every rank's arrival words.  Then either that CTA waits (acquire) until
+// every rank's word for this layer reaches the epoch -- the gathered rows are
+// complete here when the kernel ends, as after an all-gather -- or, with a deferred
+// wait, the kernel ends at once and a later peer_wait_kernel does the waiting for
+// all layers of a step together, so no layer is held up by the slowest rank.  Every
+// wait is bounded (~2 s); running out of it sets the error word and returns.  Epochs
+// only grow, so no flag is ever reset.
+//
+// A rank can write into a peer's gathered buffer while that peer still reads the
+// same rows from an earlier call; callers that reuse buffers alternate two of them
+// (the Python stack does, by step parity).
 constexpr long long kPeerWaitNs = 2000000000ll;
 
 __device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
@@ -214,16 +206,37 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
+// Waits (bounded) until all `world` words at `flags` reach `epoch`; false on timeout.
+__device__ bool wait_arrivals(const uint32_t* flags, int world, uint32_t epoch) {
+    const unsigned long long t0 = global_ns();
+    for (int j = 0; j < world; ++j) {
+        while (static_cast<int32_t>(load_acquire_sys(flags + j) - epoch) < 0) {
+            if (global_ns() - t0 > static_cast<unsigned long long>(kPeerWaitNs)) return false;
+            __nanosleep(256);
+        }
+    }
+    return true;
+}
+
 template <int DPT, typename T>
 __device__ void peer_gather_rows(const AttnParams& p, int64_t row, const float (&o)[DPT], float inv) {
-    const int64_t dst_row = static_cast<int64_t>(p.rank) * p.B * p.QH + row;
-    for (int j = 0; j < p.world; ++j) {
-        T* dst = static_cast<T*>(p.peer_out[j]) + dst_row * p.D;
+    // Stage the row in shared memory, then store it to every rank as 16-byte chunks
+    // (head_dim is a multiple of 8, so a row is a whole number of chunks).
+    __shared__ __align__(16) T s_row[256];
 #pragma unroll
-        for (int c = 0; c < DPT; ++c) {
-            const int d = threadIdx.x + 128 * c;
-            if (d < p.D) dst[d] = from_float<T>(o[c] * inv);
-        }
+    for (int c = 0; c < DPT; ++c) {
+        const int d = threadIdx.x + 128 * c;
+        if (d < p.D) s_row[d] = from_float<T>(o[c] * inv);
+    }
+    __syncthreads();
+    const int chunks = p.D * static_cast<int>(sizeof(T)) / 16;
+    const int64_t dst_row = static_cast<int64_t>(p.rank) * p.B * p.QH + row;
+    const uint4* src = reinterpret_cast<const uint4*>(s_row);
+    for (int i = threadIdx.x; i < p.world * chunks; i += blockDim.x) {
+        const int j = i / chunks;
+        const int c = i - j * chunks;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[j]) + dst_row * p.D);
+        dst[c] = src[c];
     }
     __syncthreads();
     if (threadIdx.x != 0) return;
@@ -235,16 +248,21 @@ __device__ void peer_gather_rows(const AttnParams& p, int64_t row, const float (
     const uint32_t epoch = p.sync[1] + 1u;
     p.sync[1] = epoch;
     for (int j = 0; j < p.world; ++j) store_release_sys(p.peer_flags[j] + p.rank, epoch);
-    const uint32_t* mine = p.peer_flags[p.rank];
-    const unsigned long long t0 = global_ns();
-    for (int j = 0; j < p.world; ++j) {
-        while (static_cast<int32_t>(load_acquire_sys(mine + j) - epoch) < 0) {
-            if (global_ns() - t0 > static_cast<unsigned long long>(kPeerWaitNs)) {
-                atomicExch(p.sync + 2, 1u);
-                return;
-            }
-            __nanosleep(256);
-        }
+    if (p.peer_defer) return;
+    if (!wait_arrivals(p.peer_flags[p.rank], p.world, epoch)) atomicExch(p.sync + 2, 1u);
+}
+
+// Deferred wait of the peer all-gather: thread l waits until every rank's arrival
+// word of layer l (own_flags + l * world) reaches that layer's epoch (sync + 3 l + 1,
+// written by the combine kernels queued before this one); a wait that runs out sets
+// the layer's error word.
+__global__ void peer_wait_kernel(const uint32_t* own_flags, uint32_t* sync, int layers, int world) {
+    pdl_trigger();
+    pdl_wait();
+    for (int l = threadIdx.x; l < layers; l += blockDim.x) {
+        const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(sync + 3 * l + 1);
+        if (!wait_arrivals(own_flags + static_cast<int64_t>(l) * world, world, epoch))
+            atomicExch(sync + 3 * l + 2, 1u);
     }
 }
 
@@ -258,7 +276,6 @@ template <typename T, int CH>  // CH = splits per chunk: 64 (head_dim <= 128) or
 __global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
     pdl_trigger();
     pdl_wait();
-    COMB_MARK(0);
     constexpr int DPT = CH == 64 ? 1 : 2;  // channels per thread (tid, tid + 128)
     const int64_t row = blockIdx.x;        // b*QH + qh
     const int S = p.S, D = p.D;
@@ -324,7 +341,6 @@ __global__ void __launch_bounds__(128) combine_kernel(AttnParams p) {
         if (d < D) out[row * D + d] = from_float<T>(o[c] * inv);
     }
     if (p.world > 1) peer_gather_rows<DPT, T>(p, row, o, inv);
-    COMB_MARK(1);
 }
 
 template <typename T>
@@ -474,11 +490,9 @@ __global__ void __launch_bounds__(kAttnThreads, kMmaCtasPerSm) attention_mma_ker
     const int64_t seg = segment_len(L, p.S);
     const int64_t lo = imin64(static_cast<int64_t>(s) * seg, L + 1);
     const int64_t hi = imin64(lo + seg, L + 1);
-    ATTN_MARK(0);
     const int64_t qrow0 = static_cast<int64_t>(b) * p.QH + static_cast<int64_t>(kvh) * p.G;
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
                                     p.dense != 0);
-    ATTN_MARK(1);
 
     const T* kc = static_cast<const T*>(p.kc);
     const T* vc = static_cast<const T*>(p.vc);
@@ -618,7 +632,6 @@ __global__ void __launch_bounds__(kAttnThreads, kMmaCtasPerSm) attention_mma_ker
         __syncwarp();
     }
     cp_async_wait<0>();
-    ATTN_MARK(2);
 #pragma unroll
     for (int nh = 0; nh < NHT; ++nh)
 #pragma unroll
@@ -673,7 +686,6 @@ __global__ void __launch_bounds__(kAttnThreads, kMmaCtasPerSm) attention_mma_ker
             p.ws_l[prow] = l;
         }
     }
-    ATTN_MARK(3);
 }
 
 // SIMT variant (fp32 caches, or head_dim outside the tensor-core instances).
@@ -703,7 +715,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_simt_kernel(AttnParams
     const int64_t hi = imin64(lo + seg, L + 1);
     const int n_union = build_union(p, b, kvh, lo, static_cast<int>(hi - lo), s_tok, s_msk, s_scan,
                                     p.dense != 0);
-    ATTN_MARK(1);
     const T* q = static_cast<const T*>(p.q);
     const T* kc = static_cast<const T*>(p.kc);
     const T* vc = static_cast<const T*>(p.vc);
@@ -846,14 +857,6 @@ int launch_simt(AttnParams p, cudaStream_t st) {
 
 using namespace popkv;
 
-#ifdef POPKV_ATTN_PROFILE
-extern "C" int attn_read_marks(unsigned long long* host, int n) {
-    return (int)cudaMemcpyFromSymbol(host, g_attn_marks, n * sizeof(unsigned long long));
-}
-extern "C" int comb_read_marks(unsigned long long* host, int n) {
-    return (int)cudaMemcpyFromSymbol(host, g_comb_marks, n * sizeof(unsigned long long));
-}
-#endif
 
 extern "C" size_t popkv_sparse_attention_workspace_bytes(int64_t batch, int64_t q_heads,
                                                          int64_t kv_heads, int64_t head_dim,
@@ -873,7 +876,8 @@ static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t
                           int64_t tokens, const int32_t* seq_len, void* out, void* workspace,
                           size_t workspace_bytes, int64_t splits, popkv_stream_t stream,
                           int mode, int world = 1, int rank = 0, void* const* peer_out = nullptr,
-                          uint32_t* const* peer_flags = nullptr, uint32_t* sync_words = nullptr) {
+                          uint32_t* const* peer_flags = nullptr, uint32_t* sync_words = nullptr,
+                          int peer_defer = 0, bool check_only = false) {
     const size_t es = dtype_size(dtype);
     if (es == 0) return fail(POPKV_ERR_UNSUPPORTED, "dtype %d is not fp32/fp16/bf16", dtype);
     if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0)
@@ -924,6 +928,7 @@ static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t
     p.world = 1;
     p.rank = 0;
     p.sync = nullptr;
+    p.peer_defer = 0;
     for (int j = 0; j < kMaxPeers; ++j) { p.peer_out[j] = nullptr; p.peer_flags[j] = nullptr; }
     if (world > 1) {
         if (world > kMaxPeers || rank < 0 || rank >= world || !peer_out || !peer_flags || !sync_words)
@@ -938,7 +943,9 @@ static int attention_impl(const void* queries, int dtype, int64_t batch, int64_t
         p.world = world;
         p.rank = rank;
         p.sync = sync_words;
+        p.peer_defer = peer_defer != 0;
     }
+    if (check_only) return POPKV_OK;  // every argument check passed; nothing launched
     const cudaStream_t st = as_stream(stream);
 
     if (mode == kFromIndices) {
@@ -996,11 +1003,25 @@ extern "C" int popkv_sparse_attention_premasked_gather(
     int cache_per_batch, const void* current_keys, const void* current_values, int64_t tokens,
     const int32_t* seq_len, void* out, void* workspace, size_t workspace_bytes, int64_t splits,
     int world, int rank, void* const* peer_out, uint32_t* const* peer_flags, uint32_t* sync_words,
-    popkv_stream_t stream) {
+    int defer_wait, popkv_stream_t stream) {
     return attention_impl(queries, dtype, batch, q_heads, head_dim, key_cache, value_cache,
                           kv_heads, kv_capacity, cache_per_batch, current_keys, current_values,
                           nullptr, 0, 2, tokens, seq_len, out, workspace, workspace_bytes, splits,
-                          stream, kPremasked, world, rank, peer_out, peer_flags, sync_words);
+                          stream, kPremasked, world, rank, peer_out, peer_flags, sync_words,
+                          defer_wait);
+}
+
+extern "C" int popkv_peer_gather_wait(const uint32_t* own_flags, uint32_t* sync_words, int layers,
+                                      int world, popkv_stream_t stream) {
+    if (layers <= 0 || world < 2 || world > kMaxPeers || !own_flags || !sync_words)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "peer wait needs layers > 0, 1 < world <= %d and "
+                    "flag / sync pointers", kMaxPeers);
+    if (!aligned(own_flags, 4) || !aligned(sync_words, 4))
+        return fail(POPKV_ERR_ALIGNMENT, "flag and sync words need 4-byte alignment");
+    const int threads = layers < 256 ? (layers + 31) / 32 * 32 : 256;
+    launch_pdl(peer_wait_kernel, dim3(1), dim3((unsigned)threads), 0, as_stream(stream), own_flags,
+               sync_words, layers, world);
+    return check_launch("popkv_peer_gather_wait");
 }
 
 extern "C" int popkv_sparse_attention_masks(void* workspace, int64_t batch, int64_t q_heads,
@@ -1073,6 +1094,14 @@ extern "C" int popkv_sparse_attention_noalloc(
                     w.total, kNoAllocScratchBytes);
     void* scratch = nullptr;
     int rc = noalloc_scratch(&scratch);
+    if (rc != POPKV_OK) return rc;
+    // Run every argument check first, so that a rejected call leaves the shared
+    // scratch (and the stream) untouched.
+    rc = attention_impl(queries, dtype, batch, q_heads, head_dim, key_cache, value_cache, kv_heads,
+                        kv_capacity, cache_per_batch, current_keys, current_values, indices,
+                        index_stride, budget, tokens, seq_len, out, scratch, kNoAllocScratchBytes, S,
+                        stream, indices ? kFromIndices : kDense, 1, 0, nullptr, nullptr, nullptr, 0,
+                        /*check_only=*/true);
     if (rc != POPKV_OK) return rc;
     // The tickets and head masks must start at zero; the array keeps whatever the
     // previous call (of any sizes) left there.

@@ -40,15 +40,6 @@ constexpr int kChunkThreads = 256;
 constexpr int kMaxChunks = 1024;  // rows up to 4M tokens on the workspace path
 constexpr int kRowThreads = 1024;
 
-// Phase timestamps for tuning builds (-DPOPKV_SELECT_PROFILE): thread 0 of each row
-// records clock64() at the phase boundaries into a device array of 16 per row.
-#ifdef POPKV_SELECT_PROFILE
-__device__ long long g_select_marks[4096 * 16];
-#define SEL_MARK(i) do { if (threadIdx.x == 0) g_select_marks[(blockIdx.y * gridDim.x + blockIdx.x) * 16 + (i)] = clock64(); } while (0)
-#else
-#define SEL_MARK(i) do { } while (0)
-#endif
-
 struct SelectShared {
     uint32_t hist[kBins];
     uint32_t wsum[32], wabove[32], wgt[32], weq[32];
@@ -347,7 +338,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_kernel(SelectArgs a) {
     const int64_t k = a.budget - 1 < L ? a.budget - 1 : L;
     const float* src = a.scores + row * a.stride;
     const RowOut r = row_output(a, row);
-    SEL_MARK(0);
     if (write_trivial(a, r, L, k, kRowThreads)) return;
 
     // 1. Lower-bound threshold from a sorted sample (rows that do not fit whole).
@@ -371,7 +361,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_kernel(SelectArgs a) {
         t0 = s[rk - 1];
         __syncthreads();
     }
-    SEL_MARK(1);
 
     // 2. Count and compact the scores >= t0 in index order (warp-contiguous segments).
     const int64_t seg = ((L + 31) / 32 + 127) / 128 * 128;
@@ -402,7 +391,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_kernel(SelectArgs a) {
     uint32_t wbase, nc;
     block_prefix<kRowThreads>(lane == 0 ? wc : 0u, sh, wbase, nc);
     wbase = __shfl_sync(0xffffffffu, wbase, 0);
-    SEL_MARK(2);
     if (nc < static_cast<uint32_t>(k) || nc > static_cast<uint32_t>(kCandMax)) {
         select_whole_row(src, L, k, sh, r);
         return;
@@ -430,14 +418,11 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_kernel(SelectArgs a) {
         base += __shfl_sync(0xffffffffu, incl, 31);
     }
     __syncthreads();
-    SEL_MARK(3);
     uint32_t thr, need;
     auto get = [&](int64_t i) { return cand_key[i]; };
     auto idx = [&](int64_t i) { return cand_idx[i]; };
     radix_threshold<kRowThreads>(get, nc, static_cast<uint32_t>(k), sh, thr, need);
-    SEL_MARK(4);
     rank_and_write<kRowThreads>(get, idx, nc, thr, need, sh, r.out, r.mask_words, r.bit);
-    SEL_MARK(5);
 }
 
 // ------------------------------------------------- workspace path: kernel 1
@@ -520,7 +505,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_finish_kernel(SelectArg
     const float* src = a.scores + row * a.stride;
     const RowOut r = row_output(a, row);
     uint32_t* hrow = a.hist + row * kBins;
-    SEL_MARK(0);
     const int64_t nchunks = (L + kChunk - 1) / kChunk;
     const uint32_t cnt = tid < nchunks ? __ldcg(a.counts + row * kMaxChunks + tid) : 0u;
     for (int i = tid; i < kBins; i += kRowThreads) {  // read, and zero for the next step
@@ -536,7 +520,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_finish_kernel(SelectArg
     block_prefix<kRowThreads>(cnt, sh, off, nc);
     if (tid < nchunks) sh.chunk_off[tid] = off;
     __syncthreads();
-    SEL_MARK(1);
     if (nc < static_cast<uint32_t>(k) || nc > static_cast<uint32_t>(kCandMax)) {
         select_whole_row(src, L, k, sh, r);
         return;
@@ -572,7 +555,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_finish_kernel(SelectArg
         }
     }
     __syncthreads();
-    SEL_MARK(2);
     uint32_t thr, need;
     auto get = [&](int64_t i) { return cand_key[i]; };
     auto idx = [&](int64_t i) { return cand_idx[i]; };
@@ -581,9 +563,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_finish_kernel(SelectArg
                                      bin << 21, 0x7ffu << 21);
     else
         radix_threshold<kRowThreads>(get, nc, static_cast<uint32_t>(k), sh, thr, need);
-    SEL_MARK(3);
     rank_and_write<kRowThreads>(get, idx, nc, thr, need, sh, r.out, r.mask_words, r.bit);
-    SEL_MARK(4);
 }
 
 
@@ -643,7 +623,6 @@ __device__ void cluster_find_bin(RowShared& sh, int slot, int nbins, uint32_t re
         sh.lane_sum[slot][lane] = l0 + l1;
     }
     if constexpr (C > 1) { cluster_arrive(); cluster_wait(); } else { __syncthreads(); }
-    SEL_MARK(5 + slot);
     if (warp == 0) {
         cg::cluster_group cluster = cg::this_cluster();
         uint32_t local = 0u;
@@ -709,7 +688,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     const int64_t lo = imin64(static_cast<int64_t>(crank) * chunk, L);
     const int n = static_cast<int>(imin64(lo + chunk, L) - lo);
     uint32_t* hrow = a.hist + row * kBins;
-    SEL_MARK(0);
 
     // Newest token, padding, and the all/nothing cases (uniform over the cluster).
     if (crank == 0) {
@@ -780,7 +758,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         }
         cluster_find_bin<C>(sh, 0, kBins, remaining);
     }
-    SEL_MARK(1);
     uint32_t prefix = sh.sel_bin << 21;
     remaining -= sh.sel_above;
 
@@ -814,7 +791,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     const uint32_t d2 = sh.sel_bin;
     prefix |= d2 << 10;
     remaining -= sh.sel_above;
-    SEL_MARK(2);
     // Digit 3 over the keys of the digit-2 bin, visiting only the top-digit bin.
     uint64_t bin2_bits = 0u;
     for (uint64_t m = bin_bits; m != 0u; m &= m - 1) {
@@ -831,7 +807,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     cluster_find_bin<C>(sh, 2, 1024, remaining);
     const uint32_t thr = prefix | sh.sel_bin;
     const uint32_t need = remaining - sh.sel_above;
-    SEL_MARK(3);
     uint64_t eq_bits = 0u;
     for (uint64_t m = bin2_bits; m != 0u; m &= m - 1) {
         const int j = __ffsll(static_cast<long long>(m)) - 1;
@@ -864,11 +839,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         sh.wsum[lane] = x - v;
         if (lane == 31) sh.total = x;
     }
-    SEL_MARK(8);
     if constexpr (C > 1) {
         cluster_arrive();
         cluster_wait();
-        SEL_MARK(9);
         if (warp == 0) {  // lane q < crank reads CTA q's totals; all loads in flight at once
             cg::cluster_group cluster = cg::this_cluster();
             const uint32_t t = lane < crank ? cluster.map_shared_rank(&sh, lane)->total : 0u;
@@ -885,7 +858,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         sh.base_eq = 0u;
     }
     __syncthreads();
-    SEL_MARK(10);
     const uint32_t before = incl - cnt + sh.wsum[warp];
     // This CTA's picks take out[P0, P0 + n_c) (index order, the slice is contiguous):
     // each thread writes its picks' token indices compacted into shared memory (over
@@ -908,13 +880,11 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         s_out[pos++] = static_cast<int32_t>(lo + first + j);
     }
     __syncthreads();
-    SEL_MARK(13);
     for (uint32_t i = tid; i < n_c; i += kRowThreads) {
         const int32_t t = s_out[i];
         if (r.out) r.out[p0 + i] = t;
         if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
     }
-    SEL_MARK(4);
     if constexpr (C > 1) cluster_wait();  // peers are done reading this CTA's shared memory
 }
 
@@ -923,11 +893,6 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
 
 using namespace popkv;
 
-#ifdef POPKV_SELECT_PROFILE
-extern "C" int sel_read_marks(long long* host, int n) {
-    return (int)cudaMemcpyFromSymbol(host, g_select_marks, n * sizeof(long long));
-}
-#endif
 
 extern "C" size_t popkv_select_workspace_bytes(int64_t rows, int64_t tokens) {
     if (rows <= 0 || tokens < 0) return 0;

@@ -332,7 +332,8 @@ at::Tensor sparse_attention_premasked(const at::Tensor& queries, const at::Tenso
                                      const c10::optional<at::Tensor>& seq_len,
                                      const at::Tensor& workspace, int64_t splits, const at::Tensor& out,
                                      std::vector<int64_t> peer_out, std::vector<int64_t> peer_flags,
-                                     int64_t rank, const c10::optional<at::Tensor>& sync_words) {
+                                     int64_t rank, const c10::optional<at::Tensor>& sync_words,
+                                     bool defer_wait) {
     for (const at::Tensor* t : {&queries, &key_cache, &value_cache, &current_keys, &current_values, &workspace, &out}) {
         CHECK_CUDA(*t); CHECK_CONTIGUOUS(*t);
     }
@@ -365,10 +366,25 @@ at::Tensor sparse_attention_premasked(const at::Tensor& queries, const at::Tenso
             value_cache.data_ptr(), kv_heads, key_cache.size(2), 1, current_keys.data_ptr(),
             current_values.data_ptr(), tokens, sl, out.data_ptr(), workspace.data_ptr(),
             (size_t)workspace.nbytes(), splits, (int)outs.size(), (int)rank, outs.data(), flags.data(),
-            reinterpret_cast<uint32_t*>(sync_words->data_ptr<int32_t>()), stream_of(queries));
+            reinterpret_cast<uint32_t*>(sync_words->data_ptr<int32_t>()), defer_wait ? 1 : 0,
+            stream_of(queries));
     }
     check_status(rc, "popkv_sparse_attention_premasked");
     return out;
+}
+
+// Deferred wait of the peer all-gather: flags = this rank's [layers, world] arrival
+// words, sync = its [layers, 3] sync words.
+void peer_wait(const at::Tensor& flags, const at::Tensor& sync) {
+    CHECK_CUDA(flags); CHECK_CONTIGUOUS(flags); CHECK_DTYPE(flags, at::kInt);
+    CHECK_CUDA(sync); CHECK_CONTIGUOUS(sync); CHECK_DTYPE(sync, at::kInt);
+    TORCH_CHECK(flags.dim() == 2 && sync.dim() == 2 && sync.size(1) == 3 && sync.size(0) == flags.size(0),
+                "flags are [layers, world] and sync words [layers, 3]");
+    c10::cuda::CUDAGuard guard(flags.device());
+    check_status(popkv_peer_gather_wait(reinterpret_cast<const uint32_t*>(flags.data_ptr<int32_t>()),
+                                        reinterpret_cast<uint32_t*>(sync.data_ptr<int32_t>()),
+                                        (int)flags.size(0), (int)flags.size(1), stream_of(flags)),
+                 "popkv_peer_gather_wait");
 }
 
 void advance(const at::Tensor& seq_len, int64_t increment) {
@@ -402,7 +418,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("value_cache"), py::arg("tokens"), py::arg("current_keys"), py::arg("current_values"),
           py::arg("seq_len"), py::arg("workspace"), py::arg("splits"), py::arg("out"),
           py::arg("peer_out") = std::vector<int64_t>{}, py::arg("peer_flags") = std::vector<int64_t>{},
-          py::arg("rank") = 0, py::arg("sync_words") = py::none());
+          py::arg("rank") = 0, py::arg("sync_words") = py::none(), py::arg("defer_wait") = false);
+    m.def("peer_wait", &peer_wait, py::arg("flags"), py::arg("sync"));
     m.def("sparse_attention", &sparse_attention, py::arg("queries"), py::arg("key_cache"),
           py::arg("value_cache"), py::arg("indices"), py::arg("budget"), py::arg("tokens"),
           py::arg("current_keys") = py::none(), py::arg("current_values") = py::none(),

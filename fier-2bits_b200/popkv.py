@@ -137,6 +137,172 @@ def dense_attention(queries: torch.Tensor, prefix_keys: torch.Tensor, prefix_val
     return out[0]
 
 
+# ---- Quest and FIER (comparison methods of the reference, plain torch) ------
+
+@dataclass
+class QuestCache:
+    """Per-page channel bounds of one layer's keys (reference popkv.py:37-44)."""
+    page_size: int
+    token_count: int
+    sealed_pages: int
+    page_min: torch.Tensor
+    page_max: torch.Tensor
+    active_keys: torch.Tensor
+
+
+def _append_current(indices: torch.Tensor, num_tokens: int) -> torch.Tensor:
+    """Append the newest token (index num_tokens - 1) to every row (popkv.py:141-145)."""
+    newest = indices.new_full((*indices.shape[:-1], 1), num_tokens - 1, dtype=torch.long)
+    return torch.cat([indices.long(), newest], dim=-1)
+
+
+def build_quest_cache(keys: torch.Tensor, *, page_size: int, reserve_tokens: int) -> QuestCache:
+    """Quest page bounds of keys [KVH, T, D]; the open page's keys stay raw (popkv.py:150-164)."""
+    kvh, tokens, dim = (int(x) for x in keys.shape)
+    sealed = tokens // page_size
+    pages_cap = math.ceil((tokens + reserve_tokens + 1) / page_size)
+    page_min = torch.empty((kvh, pages_cap, dim), device=keys.device, dtype=torch.float32)
+    page_max = torch.empty_like(page_min)
+    if sealed:
+        paged = keys[:, : sealed * page_size].float().view(kvh, sealed, page_size, dim)
+        page_min[:, :sealed] = paged.amin(dim=2)
+        page_max[:, :sealed] = paged.amax(dim=2)
+    return QuestCache(page_size, tokens, sealed, page_min, page_max,
+                      keys[:, sealed * page_size:].detach().clone().contiguous())
+
+
+def quest_scores(queries: torch.Tensor, cache: QuestCache, current_keys: torch.Tensor,
+                 head_to_kv: torch.Tensor) -> torch.Tensor:
+    """Upper bound of q.k per page, the open page including the current key (popkv.py:167-178).
+
+    queries [QH, D], current_keys [KVH, D] -> fp32 [QH, pages].  Like the reference,
+    it writes the open page's bounds into the cache.
+    """
+    open_keys = torch.cat([cache.active_keys, current_keys[:, None].detach()], dim=1).float()
+    page = cache.sealed_pages
+    cache.page_min[:, page] = open_keys.amin(dim=1)
+    cache.page_max[:, page] = open_keys.amax(dim=1)
+    lo = cache.page_min[:, : page + 1].index_select(0, head_to_kv)
+    hi = cache.page_max[:, : page + 1].index_select(0, head_to_kv)
+    q = queries.float()[:, None]
+    return torch.maximum(q * lo, q * hi).sum(dim=-1)
+
+
+def quest_indices(scores: torch.Tensor, *, num_tokens: int, page_size: int, budget: int):
+    """Token indices of the top pages, the newest token forced in (popkv.py:181-194).
+
+    Returns (indices int64 [QH, pages*page_size], valid bool of the same shape).
+    """
+    n_pages = min(int(scores.shape[-1]), max(1, math.ceil(budget / page_size)))
+    pages = torch.topk(scores, k=n_pages, dim=-1, sorted=False).indices
+    tokens = (pages[:, :, None] * page_size + torch.arange(page_size, device=scores.device)).flatten(1)
+    valid = tokens < num_tokens
+    newest = num_tokens - 1
+    present = ((tokens == newest) & valid).any(dim=-1)
+    tokens[:, -1] = torch.where(present, tokens[:, -1], tokens.new_tensor(newest))
+    valid[:, -1] = torch.where(present, valid[:, -1], valid.new_tensor(True))
+    return tokens, valid
+
+
+def append_quest(cache: QuestCache, keys: torch.Tensor) -> None:
+    """Append keys [KVH, n, D]; a page that fills up is sealed (popkv.py:197-207)."""
+    cache.active_keys = torch.cat([cache.active_keys, keys.detach()], dim=1).contiguous()
+    cache.token_count += int(keys.shape[1])
+    if int(cache.active_keys.shape[1]) == cache.page_size:
+        page = cache.sealed_pages
+        full = cache.active_keys.float()
+        cache.page_min[:, page] = full.amin(dim=1)
+        cache.page_max[:, page] = full.amax(dim=1)
+        cache.sealed_pages += 1
+        cache.active_keys = cache.active_keys[:, :0].contiguous()
+
+
+@dataclass
+class FIERCache:
+    """FIER 1-bit packed keys with per-group channel extrema (reference popkv.py:47-55)."""
+    group_size: int
+    token_count: int
+    sealed_tokens: int
+    packed: torch.Tensor
+    group_min: torch.Tensor
+    group_max: torch.Tensor
+    active_keys: torch.Tensor
+
+
+def build_fier_cache(keys: torch.Tensor, *, group_size: int, reserve_tokens: int) -> FIERCache:
+    """Pack keys [KVH, T, D] into storage with room for the reserve (popkv.py:212-235)."""
+    import fier_torch
+    packed, mins, maxs = fier_torch.pack_keys(keys.contiguous(), group_size=group_size)
+    kvh, tokens, dim = (int(x) for x in keys.shape)
+    capacity = math.ceil((tokens + reserve_tokens) / group_size) * group_size
+    words = torch.empty((kvh, dim, math.ceil(capacity / 32)), device=keys.device, dtype=packed.dtype)
+    lo = torch.empty((kvh, math.ceil(capacity / group_size), dim), device=keys.device, dtype=mins.dtype)
+    hi = torch.empty_like(lo)
+    words[:, :, : packed.shape[2]] = packed
+    lo[:, : mins.shape[1]] = mins
+    hi[:, : maxs.shape[1]] = maxs
+    sealed = (tokens // group_size) * group_size
+    return FIERCache(group_size, tokens, sealed, words, lo, hi,
+                     keys[:, sealed:].detach().clone().contiguous())
+
+
+def stage_fier(cache: FIERCache, current_keys: torch.Tensor) -> None:
+    """Re-pack the open group with the current keys [KVH, 1, D] (popkv.py:238-247)."""
+    import fier_torch
+    open_keys = torch.cat([cache.active_keys, current_keys.detach()], dim=1).contiguous()
+    packed, mins, maxs = fier_torch.pack_keys(open_keys, group_size=cache.group_size)
+    w0 = cache.sealed_tokens // 32
+    g0 = cache.sealed_tokens // cache.group_size
+    cache.packed[:, :, w0 : w0 + packed.shape[2]] = packed
+    cache.group_min[:, g0 : g0 + mins.shape[1]] = mins
+    cache.group_max[:, g0 : g0 + maxs.shape[1]] = maxs
+
+
+def append_fier(cache: FIERCache, keys: torch.Tensor) -> None:
+    """Record appended keys [KVH, n, D]; a full group is sealed (popkv.py:250-255)."""
+    cache.active_keys = torch.cat([cache.active_keys, keys.detach()], dim=1).contiguous()
+    cache.token_count += int(keys.shape[1])
+    if int(cache.active_keys.shape[1]) == cache.group_size:
+        cache.sealed_tokens += cache.group_size
+        cache.active_keys = cache.active_keys[:, :0].contiguous()
+
+
+def fier_scores(queries: torch.Tensor, cache: FIERCache, current_keys: torch.Tensor,
+                head_to_kv: torch.Tensor, *, num_tokens: int) -> torch.Tensor:
+    """stage_fier + FIER score of queries [QH, D] over num_tokens tokens (popkv.py:575-581)."""
+    import fier_torch
+    stage_fier(cache, current_keys)
+    return fier_torch.score_packed_batched(queries[None], cache.packed, cache.group_min,
+                                           cache.group_max, head_to_kv, tokens=num_tokens,
+                                           group_size=cache.group_size)
+
+
+def gather_selected_kv(prefix_keys, prefix_values, current_keys, current_values, indices,
+                       head_to_kv):
+    """Materialised gather of the selected rows (popkv.py:341-357), for the torch methods.
+
+    prefix [KVH, L, D], current [KVH, D], indices [QH, n] -> keys, values [QH, n, D];
+    index L selects the current row.
+    """
+    L = int(prefix_keys.shape[1])
+    clamped = indices.clamp_max(L - 1)
+    heads = head_to_kv[:, None].expand_as(clamped)
+    is_current = indices.eq(L).unsqueeze(-1)
+    keys = torch.where(is_current, current_keys.index_select(0, head_to_kv)[:, None],
+                       prefix_keys[heads, clamped])
+    values = torch.where(is_current, current_values.index_select(0, head_to_kv)[:, None],
+                         prefix_values[heads, clamped])
+    return keys, values
+
+
+def selected_attention(queries, keys, values, valid_mask=None):
+    """SDPA of queries [QH, D] over their own rows [QH, n, D] (popkv.py:360-368)."""
+    mask = None if valid_mask is None else valid_mask[None, :, None]
+    return torch.nn.functional.scaled_dot_product_attention(
+        queries[None, :, None], keys[None], values[None], attn_mask=mask, dropout_p=0.0,
+        is_causal=False)[0, :, 0]
+
+
 def shard_heads(rank: int, world: int, kv_heads: int, q_heads: int):
     """KV-head sharding: rank r owns KV heads [r*KVH/W, (r+1)*KVH/W) and their query heads."""
     if kv_heads % world or q_heads % kv_heads:
@@ -175,7 +341,7 @@ class RetrievalStack:
 
     def __init__(self, *, layers: int, batch: int, kv_heads: int, q_heads: int, head_dim: int,
                  max_tokens: int, budget: int, dtype=torch.bfloat16, device=None,
-                 process_group=None):
+                 process_group=None, gather_wait: str | None = None):
         self.device = torch.device(device or "cuda")
         self.layers, self.batch, self.head_dim, self.budget = layers, batch, head_dim, budget
         self.dtype = dtype
@@ -215,21 +381,49 @@ class RetrievalStack:
         self.v_in = torch.zeros(layers, B, H, head_dim, dtype=dtype, device=dev)
         self.out = torch.zeros(layers, B, QH, head_dim, dtype=dtype, device=dev)
         # world > 1: the attention combine all-gathers each layer's output over NVLink
-        # peer memory (symmetric buffers); POPKV_GATHER=nccl selects an NCCL
-        # all-gather after the attention instead.
+        # peer memory (symmetric buffers, two of them used by alternate steps);
+        # POPKV_GATHER=nccl selects an NCCL all-gather after the attention instead.
+        # gather_wait "step" (default): one wait for all layers at the end of the step,
+        # so no layer waits for the slowest rank; "layer": every layer's combine waits
+        # for its own rows (what a decoder whose next layer reads them needs).
         self.peer = None
-        self.gathered = None
+        self._gathered = None
+        import os
+        self.gather_wait = gather_wait or os.environ.get("POPKV_GATHER_WAIT", "step")
+        if self.gather_wait not in ("step", "layer"):
+            raise ValueError("gather_wait is 'step' or 'layer'")
         if self.world > 1:
-            import os
             if os.environ.get("POPKV_GATHER", "peer") == "nccl":
-                self.gathered = torch.zeros(layers, self.world * B, QH, head_dim, dtype=dtype, device=dev)
+                g = torch.zeros(layers, self.world * B, QH, head_dim, dtype=dtype, device=dev)
+                self._gathered = (g, g)
             else:
                 self.peer = pk.PeerGather(layers, B * QH, head_dim, dtype, group=process_group)
-                self.gathered = self.peer.gathered.view(layers, self.world * B, QH, head_dim)
-        self.graph = None
+                g = self.peer.gathered.view(2, layers, self.world * B, QH, head_dim)
+                self._gathered = (g[0], g[1])
+        self.steps_done = 0  # parity of the next step picks its gathered buffer
+        self.graphs = None
         # The append of a layer only has to follow that layer's score, so it runs on a
         # side stream in parallel with select and attention; steps join it at the end.
         self.side = torch.cuda.Stream(device=dev)
+
+    @property
+    def gathered(self):
+        """All-gathered outputs [layers, world*B, QH_l, D] of the last step (world > 1).
+
+        With the peer all-gather the buffer alternates between steps: the rows of a
+        step stay valid until the step after next is queued.
+        """
+        if self._gathered is None:
+            return None
+        return self._gathered[(self.steps_done - 1) % 2]
+
+    @property
+    def graph(self):
+        return self.graphs
+
+    @graph.setter
+    def graph(self, value):
+        self.graphs = value
 
     # ------------------------------------------------------------------ setup
     def prefill(self, layer: int, keys: torch.Tensor, values: torch.Tensor) -> None:
@@ -248,7 +442,7 @@ class RetrievalStack:
         self.seq_len.fill_(self.length)
 
     # ------------------------------------------------------------------- step
-    def _layer(self, i: int) -> None:
+    def _layer(self, i: int, parity: int) -> None:
         tokens = self.max_tokens
         pk.score(self.q_in[i], self.packed[i], head_to_kv=self.head_to_kv, tokens=tokens,
                  seq_len=self.seq_len, out=self.scores, hist=self.score_hist)
@@ -265,49 +459,70 @@ class RetrievalStack:
                                       tokens=tokens, current_keys=self.k_in[i],
                                       current_values=self.v_in[i], seq_len=self.seq_len,
                                       workspace=self.workspace[i], out=self.out[i],
-                                      gather=self.peer, layer=i)
+                                      gather=self.peer, layer=i, parity=parity,
+                                      defer_wait=self.gather_wait == "step")
         if self.world > 1 and self.peer is None:
             import torch.distributed as dist
-            dist.all_gather_into_tensor(self.gathered[i], self.out[i], group=self.group)
+            dist.all_gather_into_tensor(self._gathered[parity][i], self.out[i], group=self.group)
 
-    def _step_launches(self) -> None:
+    def _step_launches(self, parity: int) -> None:
         for i in range(self.layers):
-            self._layer(i)
+            self._layer(i, parity)
+        if self.peer is not None and self.gather_wait == "step":
+            self.peer.wait()
         torch.cuda.current_stream().wait_stream(self.side)
         pk.advance(self.seq_len, 1)
 
-    def step(self, q=None, k=None, v=None) -> torch.Tensor:
-        """One decode step over all layers. q [layers, B, QH_l, D], k/v [layers, B, KVH_l, D]."""
+    def step(self, q=None, k=None, v=None, *, check: bool = False) -> torch.Tensor:
+        """One decode step over all layers. q [layers, B, QH_l, D], k/v [layers, B, KVH_l, D].
+
+        Returns ``out`` [layers, B, QH_l, D] (one rank) or the all-gathered outputs
+        [layers, world*B, QH_l, D].  With ``check`` the call synchronises and raises
+        RuntimeError if a peer all-gather wait ran out (the gathered rows are then
+        incomplete); without it, poll ``peer_errors()``.
+        """
         if self.length + 1 > self.max_tokens:
             raise RuntimeError("Pop-KV cache reserve exhausted")
         if q is not None:
             self.q_in.copy_(q, non_blocking=True)
             self.k_in.copy_(k, non_blocking=True)
             self.v_in.copy_(v, non_blocking=True)
-        if self.graph is not None:
-            self.graph.replay()
+        parity = self.steps_done % 2
+        if self.graphs is not None:
+            self.graphs[parity].replay()
         else:
-            self._step_launches()
+            self._step_launches(parity)
         self.length += 1
+        self.steps_done += 1
+        if check and self.peer_errors():
+            raise RuntimeError(f"{self.peer_errors()} peer all-gather waits ran out: "
+                               "the gathered outputs are incomplete")
         return self.out if self.world == 1 else self.gathered
 
     def capture(self) -> None:
-        """Record one decode step as a CUDA graph (run once eagerly first to warm up)."""
-        self.graph = None
-        g = torch.cuda.CUDAGraph()
-        stream = torch.cuda.Stream()
-        stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(g, stream=stream):
-                self._step_launches()
-        torch.cuda.current_stream().wait_stream(stream)
-        # Capturing enqueued nothing: the graph is replayed by step().
-        self.graph = g
+        """Record the decode step as CUDA graphs (run once eagerly first to warm up).
+
+        Two graphs, one per gathered buffer, replayed by alternate steps.
+        """
+        self.graphs = None
+        graphs = []
+        for parity in (0, 1):
+            g = torch.cuda.CUDAGraph()
+            stream = torch.cuda.Stream()
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    self._step_launches(parity)
+            torch.cuda.current_stream().wait_stream(stream)
+            graphs.append(g)
+        # Capturing enqueued nothing: the graphs are replayed by step().
+        self.graphs = graphs
 
     def peer_errors(self) -> int:
         """Peer all-gather waits that ran out (0 on a healthy run)."""
         return 0 if self.peer is None else self.peer.errors()
 
     def launches_per_step(self) -> int:
-        # score, select, attention + combine, append per layer, + advance.
-        return self.layers * 5 + 1
+        # score, select, attention + combine, append per layer, + advance
+        # (+ the deferred peer wait).
+        return self.layers * 5 + 1 + (1 if self.peer is not None and self.gather_wait == "step" else 0)

@@ -109,12 +109,15 @@ def select(scores: torch.Tensor, *, budget: int, tokens: int | None = None,
 
 def sparse_attention_premasked(queries, key_cache, value_cache, *, tokens: int, current_keys,
                                current_values, workspace, out, seq_len=None, splits: int = 0,
-                               gather: "PeerGather | None" = None, layer: int = 0):
+                               gather: "PeerGather | None" = None, layer: int = 0,
+                               parity: int = 0, defer_wait: bool = False):
     """sparse_attention over the bitmask that ``select(attn_workspace=workspace)`` wrote.
 
     Batched caches [B, KVH, kv_cap, D]; queries/out [B, QH, D]; current rows [B, KVH, D].
     With ``gather`` (a :class:`PeerGather` of this rank), the output rows are also
-    all-gathered over NVLink peer memory into ``gather.gathered[layer]`` of every rank.
+    all-gathered over NVLink peer memory into ``gather.gathered[parity, layer]`` of
+    every rank.  With ``defer_wait`` the call only publishes its arrival and
+    ``gather.wait()`` (queued later on the stream) waits for all layers at once.
     """
     if gather is None:
         return extension().sparse_attention_premasked(queries, key_cache, value_cache, int(tokens),
@@ -123,16 +126,19 @@ def sparse_attention_premasked(queries, key_cache, value_cache, *, tokens: int, 
     return extension().sparse_attention_premasked(queries, key_cache, value_cache, int(tokens),
                                                   current_keys, current_values, seq_len,
                                                   workspace, int(splits), out,
-                                                  gather.out_ptrs(layer), gather.flag_ptrs(layer),
-                                                  gather.rank, gather.sync[layer])
+                                                  gather.out_ptrs(layer, parity), gather.flag_ptrs(layer),
+                                                  gather.rank, gather.sync[layer], bool(defer_wait))
 
 
 class PeerGather:
     """Buffers of the fused peer all-gather (one process per GPU, one NVLink domain).
 
-    ``gathered`` [layers, world * rows, head_dim] and the arrival words [layers, world]
-    live in symmetric memory (every rank maps every rank's copy); ``sync`` [layers, 3]
-    holds this rank's ticket / epoch / error words.  Built collectively by all ranks.
+    ``gathered`` [2, layers, world * rows, head_dim] and the arrival words
+    [layers, world] live in symmetric memory (every rank maps every rank's copy);
+    ``sync`` [layers, 3] holds this rank's ticket / epoch / error words.  Two gathered
+    buffers, used by alternate steps: a rank that runs ahead writes the next step's
+    rows into the other buffer, never into the rows a slower peer may still be
+    reading.  Built collectively by all ranks.
     """
 
     def __init__(self, layers: int, rows: int, head_dim: int, dtype, group=None):
@@ -143,8 +149,8 @@ class PeerGather:
         if self.world > 8:
             raise ValueError("the peer all-gather spans at most 8 ranks")
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.rows, self.head_dim = int(rows), int(head_dim)
-        self.gathered = symm_mem.empty(layers, self.world * rows, head_dim, dtype=dtype, device=dev)
+        self.layers, self.rows, self.head_dim = int(layers), int(rows), int(head_dim)
+        self.gathered = symm_mem.empty(2, layers, self.world * rows, head_dim, dtype=dtype, device=dev)
         self.flags = symm_mem.empty(layers, self.world, dtype=torch.int32, device=dev)
         self.flags.zero_()
         self.gathered.zero_()
@@ -153,7 +159,7 @@ class PeerGather:
         self._hg = symm_mem.rendezvous(self.gathered, group_name)
         self._hf = symm_mem.rendezvous(self.flags, group_name)
         self.sync = torch.zeros(layers, 3, dtype=torch.int32, device=dev)
-        self._out_stride = self.world * rows * head_dim * self.gathered.element_size()
+        self._layer_stride = self.world * rows * head_dim * self.gathered.element_size()
         self._flag_stride = self.world * 4
 
     @staticmethod
@@ -161,11 +167,16 @@ class PeerGather:
         off = tensor.data_ptr() - int(handle.buffer_ptrs[rank])  # the tensor's place in its buffer
         return [int(p) + off for p in handle.buffer_ptrs]
 
-    def out_ptrs(self, layer: int) -> list:
-        return [p + layer * self._out_stride for p in self._peer_bases(self._hg, self.gathered, self.rank)]
+    def out_ptrs(self, layer: int, parity: int = 0) -> list:
+        off = (int(parity) * self.layers + int(layer)) * self._layer_stride
+        return [p + off for p in self._peer_bases(self._hg, self.gathered, self.rank)]
 
     def flag_ptrs(self, layer: int) -> list:
         return [p + layer * self._flag_stride for p in self._peer_bases(self._hf, self.flags, self.rank)]
+
+    def wait(self) -> None:
+        """Queue the deferred wait for every layer's arrivals (current stream)."""
+        extension().peer_wait(self.flags, self.sync)
 
     def errors(self) -> int:
         return int(self.sync[:, 2].sum().item())

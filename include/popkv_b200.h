@@ -192,13 +192,20 @@ int popkv_sparse_attention_premasked(const void* queries, int dtype, int64_t bat
  * runs one GPU and has no counterpart; this serves the KV-head-sharded decode).
  * Rank `rank` of `world` (<= 8, one process per GPU) writes its out row r into row
  * rank * batch * q_heads + r of every rank's gathered buffer (peer_out[j]: rank j's
- * buffer, [world * batch * q_heads, head_dim], mapped into this process), then
- * stores this layer's epoch into word `rank` of every rank's arrival words
- * (peer_flags[j]: rank j's [world] uint32, zero-initialised once) and waits until
- * all `world` of its own words hold the epoch: on return of the stream work the
- * gathered buffer is complete on this rank.  sync_words: this rank's [3] uint32
- * (zeroed once): CTA ticket, epoch, error (1 after a wait ran out, ~2 s).  Every rank
- * must make the same sequence of calls for a given set of buffers.
+ * buffer, [world * batch * q_heads, head_dim], mapped into this process; 16-byte
+ * aligned), then stores this layer's epoch into word `rank` of every rank's arrival
+ * words (peer_flags[j]: rank j's [world] uint32, zero-initialised once).
+ *   defer_wait == 0: the call then waits until all `world` of its own words hold the
+ *     epoch: on return of the stream work the gathered buffer is complete on this rank.
+ *   defer_wait != 0: the call does not wait; popkv_peer_gather_wait, queued later on
+ *     the same stream, waits for this and every other layer of the step at once.
+ * sync_words: this rank's [3] uint32 (zeroed once): CTA ticket, epoch, error (1 after
+ * a wait ran out, ~2 s; the gathered rows are then incomplete and must not be used).
+ * Every rank must make the same sequence of calls for a given set of buffers.  A
+ * rank may write a peer's gathered rows while that peer still reads them from an
+ * earlier call of the same layer: reuse a gathered buffer no sooner than every
+ * second step (alternate two buffers), and consume a step's rows on the stream
+ * before the next step's work is queued.
  */
 int popkv_sparse_attention_premasked_gather(
     const void* queries, int dtype, int64_t batch, int64_t q_heads, int64_t head_dim,
@@ -206,7 +213,17 @@ int popkv_sparse_attention_premasked_gather(
     int cache_per_batch, const void* current_keys, const void* current_values, int64_t tokens,
     const int32_t* seq_len, void* out, void* workspace, size_t workspace_bytes, int64_t splits,
     int world, int rank, void* const* peer_out, uint32_t* const* peer_flags, uint32_t* sync_words,
-    popkv_stream_t stream);
+    int defer_wait, popkv_stream_t stream);
+/*
+ * Deferred wait of the peer all-gather (no counterpart in the reference): for every
+ * layer l < layers, waits until this rank's arrival words own_flags[l*world ..
+ * l*world + world-1] all reach the epoch that the layer's last
+ * popkv_sparse_attention_premasked_gather(defer_wait != 0) call stored in
+ * sync_words[3*l + 1].  sync_words is the [layers, 3] array of those calls' sync
+ * words; a wait that runs out (~2 s) sets sync_words[3*l + 2] to 1.
+ */
+int popkv_peer_gather_wait(const uint32_t* own_flags, uint32_t* sync_words, int layers, int world,
+                           popkv_stream_t stream);
 /* Token-bitmask region of an attention workspace (for popkv_select's head_masks). */
 int popkv_sparse_attention_masks(void* workspace, int64_t batch, int64_t q_heads,
                                  int64_t kv_heads, int64_t head_dim, int64_t tokens,
