@@ -56,12 +56,23 @@ def build_c_library(force: bool = False, verbose: bool = False) -> Path:
     LIB.mkdir(exist_ok=True)
     obj_dir = LIB / "obj"
     obj_dir.mkdir(exist_ok=True)
-    objs = []
+    objs, jobs = [], []
+    headers = [CSRC / "common.cuh", INCLUDE / "popkv_b200.h"]
     for src in CUDA_SOURCES:
         obj = obj_dir / (Path(src).stem + ".o")
-        _run([NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-              "-Xptxas", "-warn-spills", f"-I{INCLUDE}", "-c", CSRC / src, "-o", obj], verbose)
         objs.append(obj)
+        if force or _stale(obj, [CSRC / src, *headers]):
+            jobs.append([NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+                         "-Xptxas", "-warn-spills", f"-I{INCLUDE}", "-c", CSRC / src, "-o", obj])
+    # The translation units are independent: compile them concurrently.
+    procs = []
+    for cmd in jobs:
+        if verbose:
+            print(" ".join(str(c) for c in cmd), flush=True)
+        procs.append(subprocess.Popen([str(c) for c in cmd]))
+    failed = [p.args for p in procs if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     tmp = C_LIB.with_suffix(".so.tmp")
     _run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"], verbose)
     os.replace(tmp, C_LIB)
