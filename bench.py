@@ -38,6 +38,13 @@ import torch  # noqa: E402
 METRIC = "retrieval ms/decode-step per layer (score+topk+gather+attn) and HBM GB/s vs peak"
 KVH, QH, D = 8, 32, 128
 PACKED_BYTES = 48  # per token per KV head at D = 128
+WORKLOADS = {
+    1: "configs[1]: Llama-3.1-8B attention layer, 32 q / 8 kv heads, head_dim 128, bf16 cache, "
+       "group 32, one append per step",
+    3: "configs[3]: batched long-context attention-only stack, 16 sequences x 131072 tokens, "
+       "32 q / 8 kv heads, head_dim 128, bf16 cache, budget 4096, one append per step, "
+       "KV heads sharded over the GPUs",
+}
 
 
 def parse():
@@ -51,6 +58,9 @@ def parse():
     ap.add_argument("--budget", type=int, default=4096)
     ap.add_argument("--cpu-sample-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=(1, 3), default=1,
+                    help="1: configs[1] (default, weak scaling by sequence); "
+                         "3: configs[3] (16 sequences x 128K tokens, strong scaling by KV head)")
     return ap.parse_args()
 
 
@@ -153,6 +163,12 @@ def algorithmic_bytes(L, budget, B, kvh, qh, union_rows):
     return {"score": score, "select": select, "attention": attn, "append": append}
 
 
+def layer_bytes(B, kvh_local, kv_cap):
+    """Device bytes one RetrievalStack layer holds: bf16 K and V caches + packed keys."""
+    cap = (kv_cap + 31) // 32 * 32
+    return 2 * B * kvh_local * kv_cap * D * 2 + B * kvh_local * cap * PACKED_BYTES
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -171,20 +187,49 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(minutes=5))
         group = dist.group.WORLD
     layers, L0, budget = args.layers, args.context, args.budget
-    B = world  # weak scaling: one sequence per GPU, sharded by KV head
     total_steps = min(args.warmup + args.steps + 2, 64)  # distinct per-step inputs, reused cyclically
     reserve = args.warmup + 2 * args.steps + 4
+    if args.config == 3:
+        # 16 sequences x 131072 tokens, KV heads sharded over the ranks
+        # (total work fixed); as many of the 32 layers as this GPU's HBM holds.
+        B = 16
+        if args.context == 32768:
+            L0 = 131072
+        per_layer = layer_bytes(B, KVH // world, L0 + reserve + 1)
+        free = torch.cuda.mem_get_info(dev)[0] - (6 << 30)
+        layers = max(1, min(32 if args.layers == 32 else args.layers, int(free // per_layer)))
+    else:
+        B = world  # weak scaling: one sequence per GPU, sharded by KV head
     stack = popkv.RetrievalStack(layers=layers, batch=B, kv_heads=KVH, q_heads=QH, head_dim=D,
                                  max_tokens=L0 + reserve, budget=budget,
                                  dtype=torch.bfloat16, device=dev, process_group=group)
     (k0, k1), (q0, q1) = stack.kv_range, stack.q_range
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2x L2
+    pack_ms = 0.0
     gens = []
     for i in range(layers):
         syn = SyntheticLayer(kv_heads=KVH, q_heads=QH, head_dim=D, seed=1000 + i, batch=B, device=dev)
-        k, v = syn.keys_values(L0)
-        stack.prefill(i, k[:, k0:k1].bfloat16(), v[:, k0:k1].bfloat16())
+        for b in range(B):
+            # Prefill a sequence at a time (same outlier channels as the layer's queries).
+            one = SyntheticLayer(kv_heads=KVH, q_heads=QH, head_dim=D, seed=1000 + i, device=dev)
+            one.gen.manual_seed(7919 * (i + 1) + b)
+            k, v = one.keys_values(L0)
+            kb, vb = k[0, k0:k1].bfloat16().contiguous(), v[0, k0:k1].bfloat16()
+            del k, v
+            # The prefill pack of this sequence's heads, timed cold (L2 flushed).
+            packed_b = tuple(p[b].reshape(-1, stack.capacity, p.shape[-1]) for p in stack.packed[i])
+            flush.fill_(i & 0xff)
+            a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            pk.pack_keys_into(kb, packed_b, token_offset=0)
+            z.record()
+            stack.prefill(i, kb, vb, sequence=b)
+            torch.cuda.synchronize()
+            pack_ms += a.elapsed_time(z)
+            del kb, vb
         gens.append(syn)
-        del k, v
+    pack_ms /= layers
+    del flush
     stack.set_length(L0)
     # Per-step inputs, generated up front (device pool for the kernel-only timing).
     qs, ks, vs = [], [], []
@@ -315,26 +360,31 @@ def run_ours(args):
     # Union of selections per (sequence, KV head) -> attention's algorithmic bytes.
     L_now = stack.length
     union_rows = 0
+    G = stack.q_heads // stack.kv_heads
     for i in range(layers):
-        idx = stack.indices[i].view(B, stack.q_heads, budget).cpu()
-        G = stack.q_heads // stack.kv_heads
-        for b in range(B):
-            for h in range(stack.kv_heads):
-                sel = idx[b, h * G:(h + 1) * G]
-                union_rows += int(torch.unique(sel[sel >= 0]).numel())
+        # Rows of one (sequence, KV head) group are contiguous: sort each group's
+        # selections and count distinct non-negative indices.
+        idx = stack.indices[i].view(B * stack.kv_heads, G * budget).sort(dim=1).values
+        new = torch.ones_like(idx, dtype=torch.bool)
+        new[:, 1:] = idx[:, 1:] != idx[:, :-1]
+        union_rows += int((new & (idx >= 0)).sum())
     union_rows //= layers
     nbytes = algorithmic_bytes(L_now, budget, B, stack.kv_heads, stack.q_heads, union_rows)
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks.get("hbm_gbs", 6650.0))
+    # Prefill pack (once per prefix, not part of the decode step): keys in, packed out.
+    stage_ms["pack"] = pack_ms
+    nbytes["pack"] = B * stack.kv_heads * L0 * (D * 2 + PACKED_BYTES)
     stages = {n: {"ms": stage_ms[n], "bytes": nbytes[n],
                   "gbs": nbytes[n] / (stage_ms[n] * 1e-3) / 1e9,
                   "frac": nbytes[n] / (stage_ms[n] * 1e-3) / 1e9 / hbm} for n in stage_ms}
+    stages["pack"]["note"] = "one-time prefill pack per layer (all sequences), L2 flushed, not in value"
     dominant = max(("score", "select", "attention"), key=lambda n: stage_ms[n])
     traffic = None  # DRAM bytes per launch from the committed ncu summary of this workload
     try:
         for ln in (ROOT / "profiles" / "roofline_traffic_configs1.txt").read_text().splitlines():
             name, val = ln.split()[:2]
-            if name.startswith(dominant) and L0 == 32768 and world == 1:
+            if name.startswith(dominant) and L0 == 32768 and world == 1 and args.config == 1:
                 traffic = float(val)
     except Exception:
         traffic = None
@@ -367,24 +417,26 @@ def run_ours(args):
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_ms, cores = time_cpu_reference(L0, budget, args.cpu_sample_steps, 1)
-        cpu_baseline = {"value": cpu_ms, "unit": "ms", "cores": cores, "kind": "port",
-                        "sample": f"{args.cpu_sample_steps} layer-steps of configs[1] shapes "
-                                  f"(L={L0}, budget={budget}, fp32 upcast of bf16), after 1 warm-up"}
+        cpu_baseline = {"value": cpu_ms * B, "unit": "ms", "cores": cores, "kind": "port",
+                        "sample": f"{args.cpu_sample_steps} layer-steps of one sequence "
+                                  f"(L={L0}, budget={budget}, 8 KV / 32 q heads, fp32 upcast of "
+                                  f"bf16), after 1 warm-up" + (f"; x{B} sequences" if B > 1 else "")}
 
     if rank == 0:
         dom = stages[dominant]
         line = {
             "metric": METRIC, "value": ms_layer, "unit": "ms", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V/Q, 4 outlier channels x8, RoPE 5e5)",
-            "config": {"workload": "configs[1]: Llama-3.1-8B attention layer, 32 q / 8 kv heads, "
-                                   "head_dim 128, bf16 cache, group 32, one append per step",
+            "higher_is_better": False, "scaling": "weak" if args.config == 1 else "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V/Q, 4 outlier channels x8, RoPE 5e5)",
+            "config": {"workload": WORKLOADS[args.config] + (f" ({layers} of 32 layers: what one GPU holds)"
+                                                             if args.config == 3 and layers < 32 else ""),
                        "context": L0, "budget": budget, "layers_per_step": layers,
                        "sequences": B, "parallelism": (f"kv-head shards x{world}, " + ("output all-gather fused into the attention combine (NVLink peer stores)"
                                                                        if stack.peer is not None else "NCCL all-gather per layer"))
                                       if world > 1 else "none",
-                       "l2": "inputs larger than L2 (32 layers rotate through ~4.7 GB per GPU)",
+                       "l2": f"inputs larger than L2 ({layers} layers rotate through "
+                             f"{layers * layer_bytes(B, stack.kv_heads, stack.kv_capacity) / 1e9:.1f} GB per GPU)",
                        "graph": "one CUDA graph per decode step"},
             "hbm_gbs_step": step_bytes / (ms_layer * 1e-3) / 1e9,
             "stages": stages,

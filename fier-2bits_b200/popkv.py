@@ -426,15 +426,25 @@ class RetrievalStack:
         self.graphs = value
 
     # ------------------------------------------------------------------ setup
-    def prefill(self, layer: int, keys: torch.Tensor, values: torch.Tensor) -> None:
-        """keys/values [B, KVH_local, T, D] (this rank's heads); packs the prefix."""
-        T = int(keys.shape[2])
+    def prefill(self, layer: int, keys: torch.Tensor, values: torch.Tensor,
+                sequence: int | None = None) -> None:
+        """Store and pack a prefix of this rank's heads.
+
+        keys/values [B, KVH_local, T, D], or [KVH_local, T, D] for one ``sequence``
+        (long contexts are prefilled a sequence at a time).
+        """
+        T = int(keys.shape[-2])
         if T > self.max_tokens:
             raise RuntimeError("prefix longer than the stack's max_tokens")
-        self.key_cache[layer][:, :, :T].copy_(keys)
-        self.value_cache[layer][:, :, :T].copy_(values)
+        if sequence is None:
+            kc, vc, packed = self.key_cache[layer], self.value_cache[layer], self.packed[layer]
+        else:
+            kc, vc = self.key_cache[layer][sequence], self.value_cache[layer][sequence]
+            packed = tuple(p[sequence] for p in self.packed[layer])
+        kc[..., :T, :].copy_(keys)
+        vc[..., :T, :].copy_(values)
         heads = keys.reshape(-1, T, self.head_dim).contiguous()
-        packed = tuple(p.view(-1, self.capacity, p.shape[-1]) for p in self.packed[layer])
+        packed = tuple(p.reshape(-1, self.capacity, p.shape[-1]) for p in packed)
         pk.pack_keys_into(heads, packed, token_offset=0)
 
     def set_length(self, length: int) -> None:
