@@ -341,8 +341,12 @@ class RetrievalStack:
 
     def __init__(self, *, layers: int, batch: int, kv_heads: int, q_heads: int, head_dim: int,
                  max_tokens: int, budget: int, dtype=torch.bfloat16, device=None,
-                 process_group=None, gather_wait: str | None = None):
+                 process_group=None, gather_wait: str | None = None,
+                 dense_layers: tuple[int, ...] = ()):
         self.device = torch.device(device or "cuda")
+        # Layers attended densely (the reference's full_layers, popkv.py:542-551):
+        # no score/select, attention over every cached token plus the current one.
+        self.dense_layers = frozenset(int(i) for i in dense_layers)
         self.layers, self.batch, self.head_dim, self.budget = layers, batch, head_dim, budget
         self.dtype = dtype
         self.group = process_group
@@ -454,6 +458,19 @@ class RetrievalStack:
     # ------------------------------------------------------------------- step
     def _layer(self, i: int, parity: int) -> None:
         tokens = self.max_tokens
+        if i in self.dense_layers:
+            self.side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self.side):
+                pk.append_keys(self.key_cache[i], self.value_cache[i], self.k_in[i], self.v_in[i],
+                               self.packed[i], position=0, seq_len=self.seq_len,
+                               kv_heads_per_seq=self.kv_heads)
+            pk.sparse_attention(self.q_in[i], self.key_cache[i], self.value_cache[i], None,
+                                budget=2, tokens=tokens, current_keys=self.k_in[i],
+                                current_values=self.v_in[i], seq_len=self.seq_len,
+                                workspace=self.workspace[i], out=self.out[i])
+            if self.world > 1:
+                raise RuntimeError("dense layers are not sharded")
+            return
         pk.score(self.q_in[i], self.packed[i], head_to_kv=self.head_to_kv, tokens=tokens,
                  seq_len=self.seq_len, out=self.scores, hist=self.score_hist)
         self.side.wait_stream(torch.cuda.current_stream())
@@ -535,4 +552,6 @@ class RetrievalStack:
     def launches_per_step(self) -> int:
         # score, select, attention + combine, append per layer, + advance
         # (+ the deferred peer wait).
-        return self.layers * 5 + 1 + (1 if self.peer is not None and self.gather_wait == "step" else 0)
+        sparse = self.layers - len(self.dense_layers)
+        return sparse * 5 + (self.layers - sparse) * 3 + 1 + \
+            (1 if self.peer is not None and self.gather_wait == "step" else 0)

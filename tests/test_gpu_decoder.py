@@ -1,0 +1,97 @@
+"""Llama decoding on the GPU: the Pop-KV decoder paths against dense attention and
+against transformers' own forward pass (tiny random bf16 Llama, head_dim 64)."""
+import pytest
+import torch
+
+import popkv
+from decoder import GraphedDecoder, LlamaSparseDecoder
+
+pytestmark = pytest.mark.gpu
+
+CONFIG = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+              num_attention_heads=4, num_key_value_heads=2, head_dim=64, rms_norm_eps=1e-5,
+              rope_theta=500000.0, max_position_embeddings=2048, tie_word_embeddings=False)
+PREFIX = 300
+
+
+def tiny_model():
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(0)
+    cfg = LlamaConfig(**CONFIG)
+    cfg._attn_implementation = "sdpa"
+    with torch.device("cuda"):
+        model = LlamaForCausalLM(cfg)
+    for p in model.parameters():  # larger weights: attention that is not uniform
+        p.data.mul_(4.0)
+    return model.to(torch.bfloat16).eval()
+
+
+def ids(n, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, CONFIG["vocab_size"], (n,), generator=g)
+
+
+def _close(a, b, tol):
+    scale = float(b.abs().max())
+    assert float((a - b).abs().max()) <= tol * scale, (float((a - b).abs().max()), scale)
+
+
+def test_popkv_with_budget_covering_the_context_equals_full():
+    model = tiny_model()
+    tok = ids(PREFIX + 3)
+    out = {}
+    for method in ("full", "popkv"):
+        dec = LlamaSparseDecoder(model, popkv.RetrievalConfig(budget=PREFIX + 8, full_layers=(0,)))
+        pc = dec.build_prefix_cache(tok[:PREFIX])
+        caches = None if method == "full" else dec.build_retrieval_caches(pc, method=method, reserve_tokens=4)
+        kv = dec.build_static_kv_cache(pc, reserve_tokens=4)
+        logits = []
+        for s in range(3):
+            lg, diag, nk, nv = dec.decode(kv, tok[PREFIX + s], method=method, retrieval_caches=caches,
+                                          return_new_kv=True)
+            dec.append_kv(kv, nk, nv)
+            if caches is not None:
+                dec.append_retrieval_caches(caches, nk)
+            logits.append(lg)
+        out[method] = torch.stack(logits)
+    _close(out["popkv"], out["full"], 2e-2)
+
+
+def test_graphed_full_decoder_matches_transformers_forward():
+    model = tiny_model()
+    tok = ids(PREFIX)
+    dec = GraphedDecoder(model, popkv.RetrievalConfig(budget=64), max_tokens=PREFIX + 8, method="full")
+    dec.prefill(tok)
+    dec.capture()
+    seq = tok.tolist()
+    for s in range(4):
+        consumed = int(dec.token.item())
+        dec.step()
+        seq.append(consumed)
+        with torch.inference_mode():
+            want = model(torch.tensor([seq], device="cuda")).logits[0, -1].float()
+        _close(dec.logits[0], want, 3e-2)
+
+
+def test_graphed_popkv_decoder_matches_eager_popkv_decoder():
+    model = tiny_model()
+    tok = ids(PREFIX, seed=2)
+    cfg = popkv.RetrievalConfig(budget=64, full_layers=(0, 1))
+    graphed = GraphedDecoder(model, cfg, max_tokens=PREFIX + 8, method="popkv")
+    graphed.prefill(tok)
+    graphed.capture()
+    eager = LlamaSparseDecoder(model, cfg)
+    pc = eager.build_prefix_cache(tok)
+    caches = eager.build_retrieval_caches(pc, method="popkv", reserve_tokens=8)
+    kv = eager.build_static_kv_cache(pc, reserve_tokens=8)
+    for s in range(4):
+        consumed = int(graphed.token.item())
+        graphed.step()
+        lg, diag, nk, nv = eager.decode(kv, consumed, method="popkv", retrieval_caches=caches,
+                                        return_new_kv=True)
+        eager.append_kv(kv, nk, nv)
+        eager.append_retrieval_caches(caches, nk)
+        _close(graphed.logits[0], lg, 3e-2)
+        assert diag.candidate_ratio < 1.0
+    tokens = graphed.generate(3)
+    assert tokens.shape == (3,) and graphed.stack.length == PREFIX + 7
