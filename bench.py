@@ -58,8 +58,9 @@ def parse():
     ap.add_argument("--budget", type=int, default=4096)
     ap.add_argument("--cpu-sample-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=(1, 3), default=1,
+    ap.add_argument("--config", type=int, choices=(1, 2, 3), default=1,
                     help="1: configs[1] (default, weak scaling by sequence); "
+                         "2: configs[2] (32-layer Llama-3.1-8B-shaped decoder, 32K prefill, greedy decode); "
                          "3: configs[3] (16 sequences x 128K tokens, strong scaling by KV head)")
     return ap.parse_args()
 
@@ -466,6 +467,147 @@ def run_ours(args):
         os._exit(0)
 
 
+def run_decoder(args):
+    """random-init Llama-3.1-8B-shaped decoder, prefill + greedy decode.
+
+    One step = one token through all 32 layers (Pop-KV retrieval at the given budget
+    in layers 2..31, dense attention in layers 0 and 1, as the reference's
+    full_layers default), replayed as one CUDA graph.  The `full` method (dense
+    attention in every layer) is timed the same way for comparison.
+    """
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    import popkv
+    from decoder import GraphedDecoder
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--config 2 runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L0, budget = args.context, args.budget
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336,
+                      num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
+                      head_dim=128, rms_norm_eps=1e-5, rope_theta=500000.0,
+                      max_position_embeddings=L0 + args.steps + args.warmup + 64,
+                      tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (L0,), generator=g)
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    results = {}
+    clocks = None
+    for method in ("popkv", "full"):
+        dec = GraphedDecoder(model, popkv.RetrievalConfig(budget=budget),
+                             max_tokens=L0 + args.warmup + 2 * args.steps + 8, method=method)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        dec.prefill(prompt)
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        dec.step()  # eager warm-up
+        dec.capture()
+        for _ in range(args.warmup - 1):
+            dec.step()
+        torch.cuda.synchronize()
+        if method == "popkv":
+            clocks = ClockSampler(0).start()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.time()
+        a.record()
+        for _ in range(args.steps):
+            dec.step()
+        z.record()
+        torch.cuda.synchronize()
+        if method == "popkv":
+            clocks.window = (w0, time.time())
+            time.sleep(0.3)
+            clocks.stop()
+        ms_token = a.elapsed_time(z) / args.steps
+        # End to end through the public API: each step's token read back to the host.
+        host = torch.empty(1, dtype=torch.long).pin_memory()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            host.copy_(dec.step(), non_blocking=True)
+        torch.cuda.synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        entry = {"ms_per_token": ms_token, "e2e_ms_per_token": e2e_ms, "prefill_s": prefill_s}
+        if method == "popkv":
+            entry["stages"] = decoder_stage_times(dec, budget, hbm)
+        results[method] = entry
+        del dec
+        torch.cuda.empty_cache()
+    weights = sum(p.numel() * p.element_size() for p in model.parameters())
+    pop = results["popkv"]
+    line = {
+        "metric": "decode ms/token end to end (configs[2]: 32-layer Llama-3.1-8B-shaped decoder)",
+        "value": pop["ms_per_token"], "unit": "ms", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": pop["ms_per_token"], "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights, uniform random prompt ids)",
+        "config": {"workload": "configs[2]: random-init Llama-3.1-8B shapes (hidden 4096, 32 layers, "
+                               "32/8 heads, FFN 14336, vocab 128256), bf16, prefill then greedy "
+                               "decode, Pop-KV in layers 2-31, dense layers 0-1",
+                   "context": L0, "budget": budget, "graph": "one CUDA graph per token",
+                   "l2": "every token reads ~16 GB of weights (far beyond L2)"},
+        "methods": results,
+        "weight_bytes": weights,
+        "weights_hbm_gbs": weights / (pop["ms_per_token"] * 1e-3) / 1e9,
+        "clocks": clocks.summary() if clocks else None,
+        "e2e": {"value": pop["e2e_ms_per_token"], "unit": "ms", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 8},
+        "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def decoder_stage_times(dec, budget, hbm, reps=10):
+    """Per-stage device time of the retrieval path over the decoder's sparse layers."""
+    import popkv_cuda as pk
+    st = dec.stack
+    sparse = [i for i in range(st.layers) if i not in st.dense_layers]
+    tokens = st.max_tokens
+    sizes = (1, st.q_heads, st.kv_heads, st.head_dim, tokens, 0)
+
+    def run(name):
+        for i in sparse:
+            if "score" in name:
+                pk.score(st.q_in[i], st.packed[i], head_to_kv=st.head_to_kv, tokens=tokens,
+                         seq_len=st.seq_len, out=st.scores, hist=st.score_hist)
+            if "select" in name:
+                pk.select(st.scores.view(-1, st.capacity), budget=budget, tokens=tokens,
+                          seq_len=st.seq_len, rows_per_seq=st.q_heads, out=st.indices[i],
+                          attn_workspace=st.workspace[i], attn_sizes=sizes, hist=st.score_hist)
+            if "attention" in name:
+                pk.sparse_attention_premasked(st.q_in[i], st.key_cache[i], st.value_cache[i],
+                                              tokens=tokens, current_keys=st.k_in[i],
+                                              current_values=st.v_in[i], seq_len=st.seq_len,
+                                              workspace=st.workspace[i], out=st.out[i])
+
+    timed = {}
+    for name in ("score", "score+select", "score+select+attention"):
+        run(name)
+        torch.cuda.synchronize()
+        st.score_hist.zero_()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            run(name)
+        z.record()
+        torch.cuda.synchronize()
+        st.score_hist.zero_()  # a score-only pass leaves its histograms behind
+        timed[name] = a.elapsed_time(z) / (reps * len(sparse))
+    run("attention")  # clears the masks the score+select runs left
+    torch.cuda.synchronize()
+    return {"score_ms": timed["score"], "topk_ms": timed["score+select"] - timed["score"],
+            "gather_attention_ms": timed["score+select+attention"] - timed["score+select"],
+            "per": f"sparse layer ({len(sparse)} per token); gather is fused into attention"}
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -494,6 +636,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 2:
+        run_decoder(args)
     else:
         run_ours(args)
 

@@ -77,7 +77,126 @@ struct PackedRow {
     }
 };
 
-template <typename TQ, int W, bool VEC>
+// One token's score against one packed query head: the word-ordered sum of
+//   fmaf(ql*kl, Cs, fmaf(dq*kl, Cq, fmaf(ql*dk, Ck, dq*dk*Cqk)))
+// (popkv_ext.cu:155-176).  pkm holds popc of the token's magnitude words (a byte per
+// word, W <= 4).  FULL: every word holds 32 channels (head_dim % 32 == 0), so no
+// lane mask is applied.
+template <int W, bool FULL>
+__device__ __forceinline__ float token_score(const uint32_t (&ks)[W], const uint32_t (&km_raw)[W],
+                                             const float (&klf)[W], const float (&kdf)[W],
+                                             uint32_t pkm, const uint32_t (&qs)[W],
+                                             const uint32_t (&qm)[W], const float (&ql)[W],
+                                             const float (&dq)[W], const int (&pq)[W],
+                                             uint32_t last_valid, int last_bits) {
+    float score = 0.0f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+        const bool edge = !FULL && w == W - 1;
+        const uint32_t km = edge ? (km_raw[w] & last_valid) : km_raw[w];
+        const uint32_t match = edge ? (~(qs[w] ^ ks[w]) & last_valid) : ~(qs[w] ^ ks[w]);
+        const uint32_t both = qm[w] & km;
+        const int cs = 2 * __popc(match) - (edge ? last_bits : 32);
+        const int pk = W <= 4 ? static_cast<int>((pkm >> (8 * w)) & 0xffu) : __popc(km);
+        const int ck = 2 * __popc(match & km) - pk;
+        const int cq = 2 * __popc(match & qm[w]) - pq[w];
+        const int cqk = 2 * __popc(match & both) - __popc(both);
+        const float kl = klf[w];
+        const float dk = kdf[w];
+        const float inner = __fmul_rn(__fmul_rn(dq[w], dk), small_int_to_float(cqk));
+        const float gs = fmaf(__fmul_rn(ql[w], kl), small_int_to_float(cs),
+                              fmaf(__fmul_rn(dq[w], kl), small_int_to_float(cq),
+                                   fmaf(__fmul_rn(ql[w], dk), small_int_to_float(ck), inner)));
+        score = __fadd_rn(score, gs);
+    }
+    return score;
+}
+
+template <int W>
+__device__ __forceinline__ void half_words(const uint16_t (&bits)[W], float (&out)[W]) {
+#pragma unroll
+    for (int w = 0; w < W; ++w) out[w] = __half2float(__ushort_as_half(bits[w]));
+}
+
+template <int W>
+__device__ __forceinline__ uint32_t mag_popcounts(const uint32_t (&km)[W], uint32_t last_valid) {
+    uint32_t p = 0u;
+    if constexpr (W <= 4) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+            const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
+            p |= static_cast<uint32_t>(__popc(km[w] & valid)) << (8 * w);
+        }
+    }
+    return p;
+}
+
+// Packs the nh query heads listed in s_heads (one warp per head): ballots give the
+// sign/magnitude words; lane j then sums word j's magnitudes in channel order (the
+// reference's sequential query sums, popkv_ext.cu:129-138) from a conflict-free
+// shared scratch.  Caller synchronises before and after.
+template <typename TQ, int W, int NWARPS>
+__device__ __forceinline__ void pack_query_heads(const TQ* __restrict__ queries, int64_t b,
+                                                 int q_heads, int D, const int* s_heads, int nh,
+                                                 float* s_abs, uint32_t* s_qs, uint32_t* s_qm,
+                                                 float* s_ql, float* s_qd, bool ref_div) {
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    float* my_abs = s_abs + warp * (W * 33);  // word j at 33 j: conflict-free column reads
+    for (int slot = warp; slot < nh; slot += NWARPS) {
+        const TQ* q = queries + (b * q_heads + s_heads[slot]) * D;
+        float v[W];
+        float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const int c = 32 * j + lane;
+            v[j] = c < D ? to_float<TQ>(q[c]) : 0.0f;
+            if (c < D) { mn = fminf(mn, v[j]); mx = fmaxf(mx, v[j]); }
+            my_abs[33 * j + lane] = fabsf(v[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        const float neg = mn * 0.5f, pos = mx * 0.5f;
+        uint32_t my_sw = 0u, my_mw = 0u;
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const bool valid = 32 * j + lane < D;
+            const bool sg = valid && v[j] >= 0.0f;
+            const bool mg = valid && (sg ? v[j] > pos : v[j] < neg);
+            const uint32_t sw = __ballot_sync(0xffffffffu, sg);
+            const uint32_t mw = __ballot_sync(0xffffffffu, mg);
+            if (lane == j) { my_sw = sw; my_mw = mw; }
+        }
+        __syncwarp();
+        if (lane < W) {
+            // Channel-order sums without branches: each magnitude goes to both sums, as
+            // itself or as +0 (which leaves a sum of magnitudes unchanged); channels past
+            // D hold 0.
+            float ls = 0.0f, hs = 0.0f;
+            const int n = min(32, D - 32 * lane);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float x = my_abs[33 * lane + i];
+                const bool high = (my_mw >> i) & 1u;
+                hs += high ? x : 0.0f;
+                ls += high ? 0.0f : x;
+            }
+            const int hc = __popc(my_mw), lc = n - hc;
+            float low, high;
+            representatives(ls, lc, hs, hc, ref_div, low, high);
+            s_qs[slot * W + lane] = my_sw;
+            s_qm[slot * W + lane] = my_mw;
+            s_ql[slot * W + lane] = low;
+            s_qd[slot * W + lane] = high - low;
+        }
+        __syncwarp();
+    }
+}
+
+template <typename TQ, int W, bool VEC, bool FULL>
 __global__ void __launch_bounds__(kScoreThreads, 2)
 score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
              const int32_t* __restrict__ k_sign, const int32_t* __restrict__ k_mag,
@@ -135,79 +254,25 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
     const int nh = s_nh;
     const bool use_hist = score_hist != nullptr && nh <= hist_heads;
 
-    // 3. Warp-parallel query pack, one warp per query head: ballots give the bit
-    // words; lane j then sums word j's magnitudes in channel order from shared memory.
+    // 3. Warp-parallel query pack, one warp per query head.
     if (use_hist)
         for (int i = tid; i < nh * kBins; i += kScoreThreads) s_hist[i] = 0u;
-    float* my_abs = s_abs + warp * (W * 33);  // word j at 33 j: conflict-free column reads
-    for (int slot = warp; slot < nh; slot += kScoreThreads / 32) {
-        const TQ* q = queries + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * D;
-        float v[W];
-        float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-            const int c = 32 * j + lane;
-            v[j] = c < D ? to_float<TQ>(q[c]) : 0.0f;
-            if (c < D) { mn = fminf(mn, v[j]); mx = fmaxf(mx, v[j]); }
-            my_abs[33 * j + lane] = fabsf(v[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        }
-        const float neg = mn * 0.5f, pos = mx * 0.5f;
-        uint32_t my_sw = 0u, my_mw = 0u;
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-            const bool valid = 32 * j + lane < D;
-            const bool sg = valid && v[j] >= 0.0f;
-            const bool mg = valid && (sg ? v[j] > pos : v[j] < neg);
-            const uint32_t sw = __ballot_sync(0xffffffffu, sg);
-            const uint32_t mw = __ballot_sync(0xffffffffu, mg);
-            if (lane == j) { my_sw = sw; my_mw = mw; }
-        }
-        __syncwarp();
-        if (lane < W) {
-            // Channel-order sums without branches: each magnitude goes to both sums, as
-            // itself or as +0 (which leaves a sum of magnitudes unchanged); channels past
-            // D hold 0.
-            float ls = 0.0f, hs = 0.0f;
-            const int n = min(32, D - 32 * lane);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float x = my_abs[33 * lane + i];
-                const bool high = (my_mw >> i) & 1u;
-                hs += high ? x : 0.0f;
-                ls += high ? 0.0f : x;
-            }
-            const int hc = __popc(my_mw), lc = n - hc;
-            float low, high;
-            representatives(ls, lc, hs, hc, ref_div, low, high);
-            s_qs[slot * W + lane] = my_sw;
-            s_qm[slot * W + lane] = my_mw;
-            s_ql[slot * W + lane] = low;
-            s_qd[slot * W + lane] = high - low;
-        }
-        __syncwarp();
-    }
+    pack_query_heads<TQ, W, kScoreThreads / 32>(queries, b, q_heads, D, s_heads, nh, s_abs, s_qs,
+                                                 s_qm, s_ql, s_qd, ref_div);
     __syncthreads();
 
     const uint32_t last_valid = (D & 31) ? ((1u << (D & 31)) - 1u) : 0xffffffffu;
     const float sc = ref_div ? rsqrtf(static_cast<float>(D)) : scale;
     // popc of each token's magnitude words does not depend on the query head: counted
     // once per token (one byte per word, W <= 4) instead of once per head.
+    const int last_bits = __popc(last_valid);
     uint32_t pkm[kTokensPerThread];
+    float klf[kTokensPerThread][W], kdf[kTokensPerThread][W];
 #pragma unroll
     for (int j = 0; j < kTokensPerThread; ++j) {
-        pkm[j] = 0u;
-        if constexpr (W <= 4) {
-#pragma unroll
-            for (int w = 0; w < W; ++w) {
-                const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
-                pkm[j] |= static_cast<uint32_t>(__popc(rows[j].m[w] & valid)) << (8 * w);
-            }
-        }
+        pkm[j] = mag_popcounts<W>(rows[j].m, last_valid);
+        half_words<W>(rows[j].l, klf[j]);
+        half_words<W>(rows[j].d, kdf[j]);
     }
     for (int slot = 0; slot < nh; ++slot) {
         float* out = scores + (static_cast<int64_t>(b) * q_heads + s_heads[slot]) * stride;
@@ -228,26 +293,8 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
         for (int j = 0; j < kTokensPerThread; ++j) {
             const int64_t t = t_base + j * kScoreThreads + tid;
             if (t >= t_end) continue;
-            float score = 0.0f;
-#pragma unroll
-            for (int w = 0; w < W; ++w) {
-                const uint32_t valid = (w == W - 1) ? last_valid : 0xffffffffu;
-                const uint32_t km = rows[j].m[w] & valid;
-                const uint32_t match = ~(qs[w] ^ rows[j].s[w]) & valid;
-                const uint32_t both = qm[w] & km;
-                const int cs = 2 * __popc(match) - __popc(valid);
-                const int cq = 2 * __popc(match & qm[w]) - pq[w];
-                const int pk = W <= 4 ? static_cast<int>((pkm[j] >> (8 * w)) & 0xffu) : __popc(km);
-                const int ck = 2 * __popc(match & km) - pk;
-                const int cqk = 2 * __popc(match & both) - __popc(both);
-                const float kl = __half2float(__ushort_as_half(rows[j].l[w]));
-                const float dk = __half2float(__ushort_as_half(rows[j].d[w]));
-                const float inner = __fmul_rn(__fmul_rn(dq[w], dk), small_int_to_float(cqk));
-                const float gs = fmaf(__fmul_rn(ql[w], kl), small_int_to_float(cs),
-                                      fmaf(__fmul_rn(dq[w], kl), small_int_to_float(cq),
-                                           fmaf(__fmul_rn(ql[w], dk), small_int_to_float(ck), inner)));
-                score = __fadd_rn(score, gs);
-            }
+            const float score = token_score<W, FULL>(rows[j].s, rows[j].m, klf[j], kdf[j], pkm[j],
+                                               qs, qm, ql, dq, pq, last_valid, last_bits);
             const float v = __fmul_rn(score, sc);
             out[t] = v;
             if (use_hist) atomicAdd(hist + (order_key(v) >> 21), 1u);
@@ -291,8 +338,11 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
             static_cast<const TQ*>(q), (int)q_heads, D, sg, mg, lo, de, (int)kv_heads, cap,
             per_batch, h2k, tokens, seq_len, scores, stride, scale, ref_div, hist, hist_heads, tile);
     };
-    if (vec) run(score_kernel<TQ, W, true>);
-    else run(score_kernel<TQ, W, false>);
+    const bool full = D % 32 == 0;
+    if (vec && full) run(score_kernel<TQ, W, true, true>);
+    else if (vec) run(score_kernel<TQ, W, true, false>);
+    else if (full) run(score_kernel<TQ, W, false, true>);
+    else run(score_kernel<TQ, W, false, false>);
     return check_launch("popkv_score");
 }
 
