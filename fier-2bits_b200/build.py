@@ -27,7 +27,7 @@ INCLUDE = ROOT / "include"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["capi.cu", "pack.cu", "score.cu", "select.cu", "attention.cu"]
+CUDA_SOURCES = ["capi.cu", "pack.cu", "score.cu", "select.cu", "attention.cu", "decoder.cu"]
 C_LIB = LIB / "libpopkv_b200.so"
 
 

@@ -395,6 +395,49 @@ void advance(const at::Tensor& seq_len, int64_t increment) {
                  "popkv_advance");
 }
 
+void rmsnorm(const at::Tensor& x, const at::Tensor& weight, double eps, const at::Tensor& out) {
+    for (const at::Tensor* t : {&x, &weight, &out}) { CHECK_CUDA((*t)); CHECK_CONTIGUOUS((*t)); }
+    TORCH_CHECK(x.scalar_type() == weight.scalar_type() && x.scalar_type() == out.scalar_type(),
+                "rmsnorm tensors must share a dtype");
+    const int64_t n = x.size(-1);
+    TORCH_CHECK(weight.numel() == n && out.numel() == x.numel(), "rmsnorm shapes");
+    c10::cuda::CUDAGuard guard(x.device());
+    check_status(popkv_rmsnorm(x.data_ptr(), weight.data_ptr(), out.data_ptr(), dtype_code(x),
+                               x.numel() / n, n, (float)eps, stream_of(x)),
+                 "popkv_rmsnorm");
+}
+
+void rope_qkv(const at::Tensor& qkv, const at::Tensor& cos, const at::Tensor& sin,
+              const at::Tensor& positions_of_rows, int64_t q_heads, int64_t kv_heads,
+              const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
+    for (const at::Tensor* t : {&qkv, &cos, &sin, &positions_of_rows, &q, &k, &v}) {
+        CHECK_CUDA((*t)); CHECK_CONTIGUOUS((*t));
+    }
+    CHECK_DTYPE(positions_of_rows, at::kInt);
+    const int64_t D = cos.size(-1);
+    const int64_t rows = qkv.numel() / ((q_heads + 2 * kv_heads) * D);
+    TORCH_CHECK(rows * (q_heads + 2 * kv_heads) * D == qkv.numel() && positions_of_rows.numel() >= rows,
+                "qkv must be [rows, (q_heads + 2 kv_heads) * head_dim]");
+    TORCH_CHECK(q.numel() == rows * q_heads * D && k.numel() == rows * kv_heads * D &&
+                v.numel() == rows * kv_heads * D && sin.sizes() == cos.sizes(), "rope output shapes");
+    c10::cuda::CUDAGuard guard(qkv.device());
+    check_status(popkv_rope_qkv(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                positions_of_rows.data_ptr<int32_t>(), cos.size(0), dtype_code(qkv), rows,
+                                q_heads, kv_heads, D, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                stream_of(qkv)),
+                 "popkv_rope_qkv");
+}
+
+void silu_mul(const at::Tensor& gate_up, const at::Tensor& out) {
+    CHECK_CUDA(gate_up); CHECK_CONTIGUOUS(gate_up); CHECK_CUDA(out); CHECK_CONTIGUOUS(out);
+    const int64_t ffn = out.size(-1);
+    TORCH_CHECK(gate_up.size(-1) == 2 * ffn && gate_up.numel() == 2 * out.numel(), "gate_up is [rows, 2 ffn]");
+    c10::cuda::CUDAGuard guard(out.device());
+    check_status(popkv_silu_mul(gate_up.data_ptr(), out.data_ptr(), dtype_code(out), out.numel() / ffn, ffn,
+                                stream_of(out)),
+                 "popkv_silu_mul");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -430,5 +473,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         return (int64_t)popkv_select_workspace_bytes(rows, tokens);
     });
     m.def("advance", &advance);
+    m.def("rmsnorm", &rmsnorm);
+    m.def("rope_qkv", &rope_qkv);
+    m.def("silu_mul", &silu_mul);
     m.def("version", &popkv_version);
 }

@@ -370,6 +370,16 @@ class GraphedDecoder:
         probe = torch.zeros(1, 1, self.hidden_size, device=self.device, dtype=self.dtype)
         cos, sin = self.backbone.rotary_emb(probe, pos)
         self.cos, self.sin = cos[0].contiguous(), sin[0].contiguous()  # [P, D]
+        self.eps = float(cfg.rms_norm_eps)
+        hs, dt, dev = self.hidden_size, self.dtype, self.device
+        # Static activations of the graphed step.
+        self.h = torch.zeros(1, hs, dtype=dt, device=dev)
+        self.h2 = torch.zeros(1, hs, dtype=dt, device=dev)
+        self.x = torch.zeros(1, hs, dtype=dt, device=dev)
+        self.qkv = torch.zeros(1, (self.H + 2 * self.KVH) * self.D, dtype=dt, device=dev)
+        self.gu = torch.zeros(1, 2 * self.ffn, dtype=dt, device=dev)
+        self.act = torch.zeros(1, self.ffn, dtype=dt, device=dev)
+        self.logits_lp = torch.zeros(1, int(cfg.vocab_size), dtype=dt, device=dev)
         self.token = torch.zeros(1, dtype=torch.long, device=self.device)
         self.logits = torch.zeros(1, int(cfg.vocab_size), dtype=torch.float32, device=self.device)
         self.graph = None
@@ -393,31 +403,28 @@ class GraphedDecoder:
 
     # ---------------------------------------------------------------- step
     def _step_body(self) -> None:
+        import popkv_cuda as pk
         st = self.stack
-        H, KVH, D = self.H, self.KVH, self.D
-        h = self.backbone.embed_tokens(self.token).view(1, self.hidden_size)
-        pos = st.seq_len.long()
-        cos = self.cos.index_select(0, pos).view(1, 1, D)
-        sin = self.sin.index_select(0, pos).view(1, 1, D)
+        H, KVH, D, hs = self.H, self.KVH, self.D, self.hidden_size
+        h = self.h
+        torch.index_select(self.backbone.embed_tokens.weight, 0, self.token, out=h)
         for i, layer in enumerate(self.backbone.layers):
-            x = layer.input_layernorm(h)
-            qkv = torch.matmul(x, self.w_qkv[i].t())
-            q = qkv[:, : H * D].view(1, H, D)
-            k = qkv[:, H * D: (H + KVH) * D].view(1, KVH, D)
-            v = qkv[:, (H + KVH) * D:].view(1, KVH, D)
-            torch.add(q * cos, _rotate_half(q) * sin, out=st.q_in[i])
-            torch.add(k * cos, _rotate_half(k) * sin, out=st.k_in[i])
-            st.v_in[i].copy_(v)
+            pk.rmsnorm(h, layer.input_layernorm.weight, self.eps, self.x)
+            torch.matmul(self.x, self.w_qkv[i].t(), out=self.qkv)
+            pk.rope_qkv(self.qkv, self.cos, self.sin, st.seq_len, q_heads=H, kv_heads=KVH,
+                        q=st.q_in[i], k=st.k_in[i], v=st.v_in[i])
             st._layer(i, 0)
-            h = torch.addmm(h, st.out[i].view(1, H * D), layer.self_attn.o_proj.weight.t())
-            y = layer.post_attention_layernorm(h)
-            gu = torch.matmul(y, self.w_gate_up[i].t())
-            a = F.silu(gu[:, : self.ffn]) * gu[:, self.ffn:]
-            h = torch.addmm(h, a, layer.mlp.down_proj.weight.t())
-        self.logits.copy_(self.model.lm_head(self.backbone.norm(h)).float())
+            torch.addmm(h, st.out[i].view(1, H * D), layer.self_attn.o_proj.weight.t(), out=self.h2)
+            pk.rmsnorm(self.h2, layer.post_attention_layernorm.weight, self.eps, self.x)
+            torch.matmul(self.x, self.w_gate_up[i].t(), out=self.gu)
+            pk.silu_mul(self.gu, self.act)
+            torch.addmm(self.h2, self.act, layer.mlp.down_proj.weight.t(), out=h)
+        pk.rmsnorm(h, self.backbone.norm.weight, self.eps, self.x)
+        torch.matmul(self.x, self.model.lm_head.weight.t(), out=self.logits_lp)
+        self.logits.copy_(self.logits_lp)
         torch.argmax(self.logits, dim=-1, out=self.token)
         torch.cuda.current_stream().wait_stream(st.side)
-        popkv.pk.advance(st.seq_len, 1)
+        pk.advance(st.seq_len, 1)
 
     @torch.inference_mode()
     def capture(self) -> None:

@@ -243,3 +243,22 @@ def retrieve(queries: torch.Tensor, packed, key_cache: torch.Tensor, value_cache
                            tokens=tokens, current_keys=current_keys,
                            current_values=current_values, seq_len=seq_len, workspace=workspace)
     return out, indices
+
+
+# ---- decoder plumbing (fused elementwise steps of a Llama decode step) --------
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
+    """out = weight * round(x * rsqrt(mean(x^2) + eps)) over the last dimension (LlamaRMSNorm)."""
+    extension().rmsnorm(x, weight, float(eps), out)
+    return out
+
+
+def rope_qkv(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, positions: torch.Tensor, *,
+             q_heads: int, kv_heads: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """Split a fused [q | k | v] row per sequence, rotate q and k at positions[b]."""
+    extension().rope_qkv(qkv, cos, sin, positions, int(q_heads), int(kv_heads), q, k, v)
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out = round(silu(gate)) * up for gate_up = [gate | up] (LlamaMLP)."""
+    extension().silu_mul(gate_up, out)
+    return out

@@ -257,6 +257,29 @@ int popkv_sparse_attention_noalloc(const void* queries, int dtype, int64_t batch
 /* Adds `increment` to seq_len[0..batch-1] on the device (end of a decode step). */
 int popkv_advance(int32_t* seq_len, int64_t batch, int32_t increment, popkv_stream_t stream);
 
+/*
+ * Decoder plumbing (fp16/bf16).  No retrieval-path counterpart in the reference; they
+ * fuse the elementwise steps the reference's decoder runs as transformers module
+ * calls (LlamaRMSNorm, apply_rotary_pos_emb, LlamaMLP act_fn * up; popkv.py:529-616)
+ * so that a graphed decode step needs one launch per step.
+ *
+ * popkv_rmsnorm: out[r] = weight * round(x[r] * rsqrt(mean(x[r]^2) + eps)), rows x n.
+ * popkv_rope_qkv: qkv [rows, (q_heads + 2 kv_heads) * head_dim] (a fused projection);
+ *   row r is rotated at position positions_of_rows[r] (device int32, clamped to the
+ *   table) with cos/sin tables [positions, head_dim]; q [rows, q_heads, head_dim],
+ *   k and v [rows, kv_heads, head_dim] are written.
+ * popkv_silu_mul: gate_up [rows, 2 ffn] = [gate | up] -> out [rows, ffn] =
+ *   round(silu(gate)) * up.
+ */
+int popkv_rmsnorm(const void* x, const void* weight, void* out, int dtype, int64_t rows, int64_t n,
+                  float eps, popkv_stream_t stream);
+int popkv_rope_qkv(const void* qkv, const void* cos_table, const void* sin_table,
+                   const int32_t* positions_of_rows, int64_t positions, int dtype, int64_t rows,
+                   int64_t q_heads, int64_t kv_heads, int64_t head_dim, void* q, void* k, void* v,
+                   popkv_stream_t stream);
+int popkv_silu_mul(const void* gate_up, void* out, int dtype, int64_t rows, int64_t ffn,
+                   popkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

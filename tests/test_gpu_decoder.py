@@ -95,3 +95,39 @@ def test_graphed_popkv_decoder_matches_eager_popkv_decoder():
         assert diag.candidate_ratio < 1.0
     tokens = graphed.generate(3)
     assert tokens.shape == (3,) and graphed.stack.length == PREFIX + 7
+
+
+def test_fused_decoder_steps_match_transformers_modules():
+    """rmsnorm / rope_qkv / silu_mul against LlamaRMSNorm, apply_rotary_pos_emb and
+    LlamaMLP's act_fn(gate) * up, in bf16."""
+    import popkv_cuda as pk
+    from transformers.models.llama import modeling_llama as m
+    model = tiny_model()
+    layer = model.model.layers[0]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = (torch.randn(3, CONFIG["hidden_size"], device="cuda", generator=g) * 2).bfloat16()
+    out = torch.empty_like(x)
+    pk.rmsnorm(x, layer.input_layernorm.weight, CONFIG["rms_norm_eps"], out)
+    want = layer.input_layernorm(x)
+    assert float((out.float() - want.float()).abs().max()) <= 2 ** -6 * float(want.abs().max())
+    H, KVH, D = 4, 2, 64
+    qkv = torch.randn(2, (H + 2 * KVH) * D, device="cuda", generator=g).bfloat16()
+    pos = torch.tensor([5, 1000], dtype=torch.int32, device="cuda")
+    cos, sin = model.model.rotary_emb(x[:1, None], torch.arange(2048, device="cuda")[None])
+    cos, sin = cos[0].contiguous(), sin[0].contiguous()
+    q = torch.empty(2, H, D, dtype=torch.bfloat16, device="cuda")
+    k = torch.empty(2, KVH, D, dtype=torch.bfloat16, device="cuda")
+    v = torch.empty_like(k)
+    pk.rope_qkv(qkv, cos, sin, pos, q_heads=H, kv_heads=KVH, q=q, k=k, v=v)
+    qr = qkv[:, : H * D].view(2, H, 1, D).transpose(1, 2).transpose(1, 2)
+    kr = qkv[:, H * D: (H + KVH) * D].view(2, KVH, 1, D)
+    c, s = cos[pos.long()][:, None], sin[pos.long()][:, None]
+    wq, wk = m.apply_rotary_pos_emb(qr, kr, c, s)
+    torch.testing.assert_close(q, wq[:, :, 0], rtol=0, atol=0)
+    torch.testing.assert_close(k, wk[:, :, 0], rtol=0, atol=0)
+    torch.testing.assert_close(v, qkv[:, (H + KVH) * D:].view(2, KVH, D), rtol=0, atol=0)
+    gu = torch.randn(3, 2 * 512, device="cuda", generator=g).bfloat16()
+    act = torch.empty(3, 512, dtype=torch.bfloat16, device="cuda")
+    pk.silu_mul(gu, act)
+    want = torch.nn.functional.silu(gu[:, :512]) * gu[:, 512:]
+    assert float((act.float() - want.float()).abs().max()) <= 2 ** -7 * float(want.abs().max())

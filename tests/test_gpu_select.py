@@ -115,3 +115,26 @@ def test_select_threshold_among_negative_infinities(L, budget):
     scores = torch.randn(3, L, generator=g)
     scores[:, ::2] = float("-inf")
     _check(scores, budget)
+
+
+@pytest.mark.parametrize("B,L", [(10, 50000), (16, 131072)])
+def test_select_many_rows_with_histogram_is_exact(B, L):
+    """Batches whose rows fill the GPU many times over take the 512-thread cluster
+    path (the configs[3] shape at B=16, L=128K): identical to the oracle's selection."""
+    KVH, G, D, budget = 8, 4, 128, 4096
+    QH = KVH * G
+    g = torch.Generator(device=DEV).manual_seed(B)
+    scores = (torch.randn(B * QH, L, generator=g, device=DEV) * 3).round(decimals=2) + 0.0  # ties; no -0
+    hist = pk.new_select_workspace(B * QH, L, DEV)
+    # The histogram the scorer would have built: counts of the top 11 key bits.
+    u = scores.contiguous().view(torch.int32)
+    key = torch.where(u < 0, ~u, u | torch.iinfo(torch.int32).min)
+    top = ((key >> 21) & 0x7ff).long()
+    h = torch.zeros(B * QH, 2048, dtype=torch.int64, device=DEV).scatter_add_(1, top, torch.ones_like(top))
+    hist[: B * QH * 2048 * 4].view(torch.int32).copy_(h.view(-1).to(torch.int32))
+    got = pk.select(scores, budget=budget, hist=hist)
+    ref = pk.select(scores, budget=budget)
+    torch.testing.assert_close(got, ref, rtol=0, atol=0)
+    assert int(hist[: B * QH * 2048 * 4].abs().sum()) == 0
+    rows = [0, B * QH // 2, B * QH - 1]
+    np.testing.assert_array_equal(ref[rows].cpu().numpy(), O.select(scores[rows].cpu().numpy(), budget=budget))
