@@ -593,7 +593,10 @@ struct RowShared {
     uint32_t total;            // this CTA's packed (> thr) << 16 | (== thr), read by peers
     uint32_t sel_bin, sel_above, count;
     uint32_t base_gt, base_eq;
+    uint64_t bar;              // completion of the bulk copy of this CTA's scores
 };
+
+__device__ unsigned int g_select_wait_timeouts = 0;
 
 __device__ __forceinline__ void cluster_arrive() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
@@ -671,12 +674,12 @@ __device__ void cluster_find_bin(RowShared& sh, int slot, int nbins, uint32_t re
     __syncthreads();
 }
 
-template <int C>
-__global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a, int per) {
+template <int C, int NT>
+__global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(SelectArgs a, int per) {
     pdl_trigger();
     pdl_wait();
     __shared__ __align__(16) RowShared sh;
-    extern __shared__ __align__(16) uint32_t s_keys[];  // [kRowThreads * per]
+    extern __shared__ __align__(16) uint32_t s_keys[];  // [NT * per]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int crank = C > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
     const int64_t row = blockIdx.y;
@@ -696,40 +699,59 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
             if (r.mask_words) atomicOr(r.mask_words + (L >> 1), r.bit << ((L & 1) * 16));
         }
         if (r.out)
-            for (int64_t j = k + 1 + tid; j < a.budget; j += kRowThreads) r.out[j] = -1;
+            for (int64_t j = k + 1 + tid; j < a.budget; j += NT) r.out[j] = -1;
     }
     if (k == 0 || k == L) {
         if (k == L)
-            for (int i = tid; i < n; i += kRowThreads) {
+            for (int i = tid; i < n; i += NT) {
                 const int32_t t = static_cast<int32_t>(lo + i);
                 if (r.out) r.out[t] = t;
                 if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
             }
         if constexpr (C > 1) { cluster_arrive(); cluster_wait(); }  // every CTA has read the histogram
         if (crank == 0)
-            for (int i = tid; i < kBins; i += kRowThreads) hrow[i] = 0u;
+            for (int i = tid; i < kBins; i += NT) hrow[i] = 0u;
         return;
     }
 
-    // 1. The slice's keys into shared memory, the scorer's histogram beside them.
+    // 1. The slice's scores into shared memory by one bulk copy (the TMA engine
+    // streams it while the threads set up the histograms), then turned into order
+    // keys in place; the scorer's histogram beside them.
     const float* src = a.scores + row * a.stride + lo;
-    if (a.vec) {
-        const int n4 = n >> 2;
-        for (int i = tid; i < n4; i += kRowThreads) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
-            reinterpret_cast<uint4*>(s_keys)[i] =
-                make_uint4(order_key(v.x), order_key(v.y), order_key(v.z), order_key(v.w));
-        }
-        for (int i = (n4 << 2) + tid; i < n; i += kRowThreads) s_keys[i] = order_key(__ldg(src + i));
-    } else {
-        for (int i = tid; i < n; i += kRowThreads) s_keys[i] = order_key(__ldg(src + i));
+    const int n4 = a.vec ? (n >> 2) : 0;  // slices start on 4-token boundaries
+    if (tid == 0) {
+        mbar_init(&sh.bar, 1);
+        fence_mbar_init();
     }
-    for (int i = tid; i < kPaddedBins; i += kRowThreads) {
+    __syncthreads();
+    if (tid == 0 && n4 > 0) {
+        mbar_expect_tx(&sh.bar, static_cast<uint32_t>(n4) * 16u);
+        bulk_load(s_keys, src, static_cast<uint32_t>(n4) * 16u, &sh.bar);
+    }
+    uint32_t hv[(kBins + NT - 1) / NT];
+#pragma unroll
+    for (int j = 0; j < (kBins + NT - 1) / NT; ++j) {
+        const int i = tid + j * NT;
+        hv[j] = i < kBins ? __ldcg(hrow + i) : 0u;
+    }
+    for (int i = tid; i < kPaddedBins; i += NT) {
         sh.hist[1][i] = 0u;
         sh.hist[2][i] = 0u;
         if (i % 65 == 64) sh.hist[0][i] = 0u;  // padding slots
     }
-    for (int i = tid; i < kBins; i += kRowThreads) sh.hist[0][hidx(i)] = __ldcg(hrow + i);
+#pragma unroll
+    for (int j = 0; j < (kBins + NT - 1) / NT; ++j) {
+        const int i = tid + j * NT;
+        if (i < kBins) sh.hist[0][hidx(i)] = hv[j];
+    }
+    if (n4 > 0 && !mbar_wait_bounded(&sh.bar, 0u) && tid == 0) atomicAdd(&g_select_wait_timeouts, 1u);
+    for (int i = tid; i < n4; i += NT) {
+        uint4 v = reinterpret_cast<uint4*>(s_keys)[i];
+        v.x = order_key(__uint_as_float(v.x)); v.y = order_key(__uint_as_float(v.y));
+        v.z = order_key(__uint_as_float(v.z)); v.w = order_key(__uint_as_float(v.w));
+        reinterpret_cast<uint4*>(s_keys)[i] = v;
+    }
+    for (int i = (n4 << 2) + tid; i < n; i += NT) s_keys[i] = order_key(__ldg(src + i));
     const int first = tid * per;
     const int nvalid = n - first <= 0 ? 0 : (n - first < per ? n - first : per);
     const uint32_t* mine = s_keys + first;
@@ -749,9 +771,9 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     if (sh.count == static_cast<uint32_t>(L)) {
         cluster_find_bin<1>(sh, 0, kBins, remaining);  // local: every CTA holds the totals
     } else {
-        for (int i = tid; i < kPaddedBins; i += kRowThreads) sh.hist[0][i] = 0u;
+        for (int i = tid; i < kPaddedBins; i += NT) sh.hist[0][i] = 0u;
         __syncthreads();
-        for (int i = tid; i < n; i += kRowThreads) {
+        for (int i = tid; i < n; i += NT) {
             const uint32_t d = s_keys[i] >> 21;
             const unsigned peers = __match_any_sync(__activemask(), d);
             if (lane == __ffs(peers) - 1) atomicAdd(&sh.hist[0][hidx(d)], __popc(peers));
@@ -787,7 +809,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     cluster_find_bin<C>(sh, 1, kBins, remaining);
     // Every CTA of the cluster has now read the scorer's histogram: zero it for the next step.
     if (crank == 0)
-        for (int i = tid; i < kBins; i += kRowThreads) hrow[i] = 0u;
+        for (int i = tid; i < kBins; i += NT) hrow[i] = 0u;
     const uint32_t d2 = sh.sel_bin;
     prefix |= d2 << 10;
     remaining -= sh.sel_above;
@@ -829,7 +851,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
     if (lane == 31) sh.wsum[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-        const uint32_t v = sh.wsum[lane];
+        const uint32_t v = lane < NT / 32 ? sh.wsum[lane] : 0u;
         uint32_t x = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -880,7 +902,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) select_row_kernel(SelectArgs a
         s_out[pos++] = static_cast<int32_t>(lo + first + j);
     }
     __syncthreads();
-    for (uint32_t i = tid; i < n_c; i += kRowThreads) {
+    for (uint32_t i = tid; i < n_c; i += NT) {
         const int32_t t = s_out[i];
         if (r.out) r.out[p0 + i] = t;
         if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
@@ -943,25 +965,42 @@ extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_str
         a.cidx = reinterpret_cast<int32_t*>(base + w.cidx);
         a.tokens_pad = w.tokens_pad;
         // Cluster size: the smallest power of two whose slices fit shared memory,
-        // raised while the rows still leave SMs idle.
+        // raised while the rows still leave SMs idle.  Rows that fill the GPU many
+        // times over (long batched contexts) take 512-thread CTAs instead, so that
+        // two rows' latency chains overlap on every SM.
         int C = 1;
         while (C < 8 && (tokens + C - 1) / C > (int64_t)kRowThreads * kRowMaxPer) C *= 2;
         while (C < 8 && rows * C * 2 <= num_sms() && (tokens + 2 * C - 1) / (2 * C) >= 2048) C *= 2;
+        int NT = kRowThreads;
+        if (rows * C > 2 * (int64_t)num_sms()) {
+            int C2 = 1;
+            while (C2 < 8 && (tokens + C2 - 1) / C2 > (int64_t)(kRowThreads / 2) * kRowMaxPer) C2 *= 2;
+            if ((tokens + C2 - 1) / C2 <= (int64_t)(kRowThreads / 2) * kRowMaxPer) { C = C2; NT = kRowThreads / 2; }
+        }
         const int64_t chunk = ((tokens + C - 1) / C + 3) / 4 * 4;
-        if (chunk <= (int64_t)kRowThreads * kRowMaxPer && rows <= 65535) {
-            const int per = (int)((chunk + kRowThreads - 1) / kRowThreads) | 1;  // odd
-            const size_t smem_keys = (size_t)per * kRowThreads * 4;
+        if (chunk <= (int64_t)NT * kRowMaxPer && rows <= 65535) {
+            const int per = (int)((chunk + NT - 1) / NT) | 1;  // odd
+            const size_t smem_keys = (size_t)per * NT * 4;
             auto go = [&](auto kern) {
                 cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_keys);
                 if (C > 1) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
-                launch_pdl_cluster(kern, dim3((unsigned)C, (unsigned)rows), dim3(kRowThreads), smem_keys,
+                launch_pdl_cluster(kern, dim3((unsigned)C, (unsigned)rows), dim3(NT), smem_keys,
                                    st, (unsigned)C, a, per);
             };
-            switch (C) {
-                case 1: go(select_row_kernel<1>); break;
-                case 2: go(select_row_kernel<2>); break;
-                case 4: go(select_row_kernel<4>); break;
-                default: go(select_row_kernel<8>); break;
+            if (NT == kRowThreads) {
+                switch (C) {
+                    case 1: go(select_row_kernel<1, kRowThreads>); break;
+                    case 2: go(select_row_kernel<2, kRowThreads>); break;
+                    case 4: go(select_row_kernel<4, kRowThreads>); break;
+                    default: go(select_row_kernel<8, kRowThreads>); break;
+                }
+            } else {
+                switch (C) {
+                    case 1: go(select_row_kernel<1, kRowThreads / 2>); break;
+                    case 2: go(select_row_kernel<2, kRowThreads / 2>); break;
+                    case 4: go(select_row_kernel<4, kRowThreads / 2>); break;
+                    default: go(select_row_kernel<8, kRowThreads / 2>); break;
+                }
             }
             return check_launch("popkv_select (row)");
         }
