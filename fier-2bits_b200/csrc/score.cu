@@ -23,7 +23,14 @@ namespace popkv {
 namespace {
 
 constexpr int kScoreThreads = 256;
-constexpr int kTokensPerThread = 4;
+#ifndef POPKV_SCORE_TOKENS_PER_THREAD
+#define POPKV_SCORE_TOKENS_PER_THREAD 4
+#endif
+#ifndef POPKV_SCORE_CTAS_PER_SM
+#define POPKV_SCORE_CTAS_PER_SM 2
+#endif
+constexpr int kTokensPerThread = POPKV_SCORE_TOKENS_PER_THREAD;
+constexpr int kScoreCtasPerSm = POPKV_SCORE_CTAS_PER_SM;
 constexpr int kTile = kScoreThreads * kTokensPerThread;
 constexpr int kBins = 2048;     // histogram of the top 11 bits of each score's order key
 constexpr int kHistHeads = 8;   // query heads per KV head covered by the in-CTA histogram
@@ -197,7 +204,7 @@ __device__ __forceinline__ void pack_query_heads(const TQ* __restrict__ queries,
 }
 
 template <typename TQ, int W, bool VEC, bool FULL>
-__global__ void __launch_bounds__(kScoreThreads, 2)
+__global__ void __launch_bounds__(kScoreThreads, kScoreCtasPerSm)
 score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
              const int32_t* __restrict__ k_sign, const int32_t* __restrict__ k_mag,
              const uint16_t* __restrict__ k_low, const uint16_t* __restrict__ k_delta,
@@ -319,7 +326,7 @@ int launch_score_t(const void* q, int64_t batch, int64_t q_heads, int D, const i
     // Tiles of at most kTile tokens, as many as keep two CTAs on every SM busy, so
     // that no SM gets a larger share of the tokens than the others.
     int64_t ntiles = (tokens + kTile - 1) / kTile;
-    const int64_t fill = (2 * num_sms()) / (batch * kv_heads);
+    const int64_t fill = (kScoreCtasPerSm * num_sms()) / (batch * kv_heads);
     if (fill > ntiles) ntiles = fill < tokens ? fill : tokens;
     const int tile = (int)((tokens + ntiles - 1) / ntiles);
     ntiles = (tokens + tile - 1) / tile;
