@@ -252,6 +252,36 @@ __device__ void peer_gather_rows(const AttnParams& p, int64_t row, const float (
     if (!wait_arrivals(p.peer_flags[p.rank], p.world, epoch)) atomicExch(p.sync + 2, 1u);
 }
 
+// All-gather by a separate push (deferred-wait mode): one CTA, queued on a side
+// stream after the layer's combine, stores this rank's `bytes` of output rows at
+// byte offset `dst_off` of every rank's gathered buffer (16-byte stores over NVLink),
+// makes them visible system-wide and publishes the layer's next epoch into its slot
+// of every rank's arrival words.  The compute stream never waits on NVLink.
+struct PushArgs {
+    const uint4* src;
+    uint4* dst[kMaxPeers];
+    uint32_t* flags[kMaxPeers];
+    uint32_t* sync;  // this rank's [3] words of the layer: ticket (unused), epoch, error
+    int64_t chunks;  // 16-byte chunks
+    int world, rank;
+};
+
+__global__ void __launch_bounds__(256) peer_push_kernel(PushArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t i = threadIdx.x; i < a.world * a.chunks; i += blockDim.x) {
+        const int j = static_cast<int>(i / a.chunks);
+        const int64_t c = i - static_cast<int64_t>(j) * a.chunks;
+        a.dst[j][c] = a.src[c];
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const uint32_t epoch = a.sync[1] + 1u;
+    a.sync[1] = epoch;
+    for (int j = 0; j < a.world; ++j) store_release_sys(a.flags[j] + a.rank, epoch);
+}
+
 // Deferred wait of the peer all-gather: thread l waits until every rank's arrival
 // word of layer l (own_flags + l * world) reaches that layer's epoch (sync + 3 l + 1,
 // written by the combine kernels queued before this one); a wait that runs out sets
@@ -1009,6 +1039,30 @@ extern "C" int popkv_sparse_attention_premasked_gather(
                           nullptr, 0, 2, tokens, seq_len, out, workspace, workspace_bytes, splits,
                           stream, kPremasked, world, rank, peer_out, peer_flags, sync_words,
                           defer_wait);
+}
+
+extern "C" int popkv_peer_push(const void* rows, int64_t bytes, void* const* peer_dst,
+                               uint32_t* const* peer_flags, int rank, int world,
+                               uint32_t* sync_words, popkv_stream_t stream) {
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "peer push needs 1 <= world <= %d and 0 <= rank < world", kMaxPeers);
+    if (bytes <= 0 || bytes % 16 != 0 || !aligned(rows, 16))
+        return fail(POPKV_ERR_ALIGNMENT, "peer push moves 16-byte aligned rows in whole 16-byte chunks");
+    if (!peer_dst || !peer_flags || !sync_words) return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
+    PushArgs a = {};
+    a.src = static_cast<const uint4*>(rows);
+    for (int j = 0; j < world; ++j) {
+        if (!peer_dst[j] || !aligned(peer_dst[j], 16) || !peer_flags[j])
+            return fail(POPKV_ERR_ALIGNMENT, "peer buffers must be 16-byte aligned");
+        a.dst[j] = static_cast<uint4*>(peer_dst[j]);
+        a.flags[j] = peer_flags[j];
+    }
+    a.sync = sync_words;
+    a.chunks = bytes / 16;
+    a.world = world;
+    a.rank = rank;
+    launch_pdl(peer_push_kernel, dim3(1), dim3(256), 0, as_stream(stream), a);
+    return check_launch("popkv_peer_push");
 }
 
 extern "C" int popkv_peer_gather_wait(const uint32_t* own_flags, uint32_t* sync_words, int layers,

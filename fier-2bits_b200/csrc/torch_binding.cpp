@@ -387,6 +387,27 @@ void peer_wait(const at::Tensor& flags, const at::Tensor& sync) {
                  "popkv_peer_gather_wait");
 }
 
+void peer_push(const at::Tensor& rows, std::vector<int64_t> peer_dst, std::vector<int64_t> peer_flags,
+               int64_t rank, const at::Tensor& sync_words) {
+    CHECK_CUDA(rows); CHECK_CONTIGUOUS(rows); CHECK_CUDA(sync_words); CHECK_CONTIGUOUS(sync_words);
+    CHECK_DTYPE(sync_words, at::kInt);
+    TORCH_CHECK(peer_dst.size() == peer_flags.size() && !peer_dst.empty() && peer_dst.size() <= 8,
+                "one destination and one flag pointer per rank (at most 8)");
+    TORCH_CHECK(sync_words.numel() == 3, "sync words are the layer's [3] words");
+    std::vector<void*> dst(peer_dst.size());
+    std::vector<uint32_t*> flg(peer_flags.size());
+    for (size_t j = 0; j < dst.size(); ++j) {
+        dst[j] = reinterpret_cast<void*>(peer_dst[j]);
+        flg[j] = reinterpret_cast<uint32_t*>(peer_flags[j]);
+    }
+    c10::cuda::CUDAGuard guard(rows.device());
+    check_status(popkv_peer_push(rows.data_ptr(), rows.numel() * rows.element_size(), dst.data(), flg.data(),
+                                 (int)rank, (int)dst.size(),
+                                 reinterpret_cast<uint32_t*>(sync_words.data_ptr<int32_t>()),
+                                 stream_of(rows)),
+                 "popkv_peer_push");
+}
+
 void advance(const at::Tensor& seq_len, int64_t increment) {
     CHECK_CUDA(seq_len); CHECK_CONTIGUOUS(seq_len); CHECK_DTYPE(seq_len, at::kInt);
     c10::cuda::CUDAGuard guard(seq_len.device());
@@ -473,6 +494,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         return (int64_t)popkv_select_workspace_bytes(rows, tokens);
     });
     m.def("advance", &advance);
+    m.def("peer_push", &peer_push);
     m.def("rmsnorm", &rmsnorm);
     m.def("rope_qkv", &rope_qkv);
     m.def("silu_mul", &silu_mul);

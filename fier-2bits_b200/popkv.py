@@ -409,6 +409,7 @@ class RetrievalStack:
         # The append of a layer only has to follow that layer's score, so it runs on a
         # side stream in parallel with select and attention; steps join it at the end.
         self.side = torch.cuda.Stream(device=dev)
+        self.push_stream = torch.cuda.Stream(device=dev)
 
     @property
     def gathered(self):
@@ -482,12 +483,18 @@ class RetrievalStack:
         pk.select(self.scores.view(-1, self.capacity), budget=self.budget, tokens=tokens,
                   seq_len=self.seq_len, rows_per_seq=self.q_heads, out=self.indices[i],
                   attn_workspace=self.workspace[i], attn_sizes=sizes, hist=self.score_hist)
+        push = self.peer is not None and self.gather_wait == "step"
         pk.sparse_attention_premasked(self.q_in[i], self.key_cache[i], self.value_cache[i],
                                       tokens=tokens, current_keys=self.k_in[i],
                                       current_values=self.v_in[i], seq_len=self.seq_len,
                                       workspace=self.workspace[i], out=self.out[i],
-                                      gather=self.peer, layer=i, parity=parity,
-                                      defer_wait=self.gather_wait == "step")
+                                      gather=None if push else self.peer, layer=i, parity=parity)
+        if push:
+            # The NVLink all-gather of this layer runs on its own stream: the next
+            # layer's kernels do not wait for it; the step's end waits for all layers.
+            self.push_stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self.push_stream):
+                self.peer.push(self.out[i].view(-1, self.head_dim), i, parity)
         if self.world > 1 and self.peer is None:
             import torch.distributed as dist
             dist.all_gather_into_tensor(self._gathered[parity][i], self.out[i], group=self.group)
@@ -496,6 +503,7 @@ class RetrievalStack:
         for i in range(self.layers):
             self._layer(i, parity)
         if self.peer is not None and self.gather_wait == "step":
+            torch.cuda.current_stream().wait_stream(self.push_stream)
             self.peer.wait()
         torch.cuda.current_stream().wait_stream(self.side)
         pk.advance(self.seq_len, 1)
@@ -553,5 +561,6 @@ class RetrievalStack:
         # score, select, attention + combine, append per layer, + advance
         # (+ the deferred peer wait).
         sparse = self.layers - len(self.dense_layers)
+        step_push = self.peer is not None and self.gather_wait == "step"
         return sparse * 5 + (self.layers - sparse) * 3 + 1 + \
-            (1 if self.peer is not None and self.gather_wait == "step" else 0)
+            ((self.layers + 1) if step_push else 0)

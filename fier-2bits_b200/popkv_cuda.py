@@ -174,6 +174,13 @@ class PeerGather:
     def flag_ptrs(self, layer: int) -> list:
         return [p + layer * self._flag_stride for p in self._peer_bases(self._hf, self.flags, self.rank)]
 
+    def push(self, out: torch.Tensor, layer: int, parity: int = 0) -> None:
+        """All-gather ``out`` (this rank's [rows, head_dim] rows of ``layer``) by a
+        separate one-CTA push kernel on the current stream; ``wait()`` completes it."""
+        off = self.rank * self.rows * self.head_dim * self.gathered.element_size()
+        extension().peer_push(out, [p + off for p in self.out_ptrs(layer, parity)],
+                              self.flag_ptrs(layer), self.rank, self.sync[layer])
+
     def wait(self) -> None:
         """Queue the deferred wait for every layer's arrivals (current stream)."""
         extension().peer_wait(self.flags, self.sync)

@@ -215,6 +215,18 @@ int popkv_sparse_attention_premasked_gather(
     int world, int rank, void* const* peer_out, uint32_t* const* peer_flags, uint32_t* sync_words,
     int defer_wait, popkv_stream_t stream);
 /*
+ * Peer all-gather of one layer's output rows by a separate push (no counterpart in
+ * the reference, which runs on one GPU): one CTA stores `bytes` (a multiple of 16)
+ * from `rows` to peer_dst[j] for every rank j < world (each rank's gathered buffer
+ * at this rank's row offset, peer-mapped), makes the stores visible system-wide and
+ * stores the layer's next epoch (sync_words[1] + 1, also written back) into
+ * peer_flags[j][rank].  Queued on a side stream after the layer's attention, it keeps
+ * NVLink off the compute stream; popkv_peer_gather_wait then waits for every layer.
+ */
+int popkv_peer_push(const void* rows, int64_t bytes, void* const* peer_dst,
+                    uint32_t* const* peer_flags, int rank, int world, uint32_t* sync_words,
+                    popkv_stream_t stream);
+/*
  * Deferred wait of the peer all-gather (no counterpart in the reference): for every
  * layer l < layers, waits until this rank's arrival words own_flags[l*world ..
  * l*world + world-1] all reach the epoch that the layer's last
