@@ -26,6 +26,9 @@ constexpr int kScoreThreads = 256;
 #ifndef POPKV_SCORE_TOKENS_PER_THREAD
 #define POPKV_SCORE_TOKENS_PER_THREAD 4
 #endif
+#ifndef POPKV_SCORE_HIST_AGG
+#define POPKV_SCORE_HIST_AGG 0
+#endif
 #ifndef POPKV_SCORE_CTAS_PER_SM
 #define POPKV_SCORE_CTAS_PER_SM 2
 #endif
@@ -299,12 +302,30 @@ score_kernel(const TQ* __restrict__ queries, int q_heads, int D,
 #pragma unroll
         for (int j = 0; j < kTokensPerThread; ++j) {
             const int64_t t = t_base + j * kScoreThreads + tid;
+#if POPKV_SCORE_HIST_AGG
+            // Warp-aggregated histogram update: lanes whose scores share a bin add once.
+            const bool valid = t < t_end;
+            float v = 0.0f;
+            if (valid) {
+                const float score = token_score<W, FULL>(rows[j].s, rows[j].m, klf[j], kdf[j],
+                                                         pkm[j], qs, qm, ql, dq, pq, last_valid,
+                                                         last_bits);
+                v = __fmul_rn(score, sc);
+                out[t] = v;
+            }
+            if (use_hist) {
+                const uint32_t bin = valid ? (order_key(v) >> 21) : 0xffffffffu;
+                const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+                if (valid && (peers & ((1u << lane) - 1u)) == 0u) atomicAdd(hist + bin, __popc(peers));
+            }
+#else
             if (t >= t_end) continue;
             const float score = token_score<W, FULL>(rows[j].s, rows[j].m, klf[j], kdf[j], pkm[j],
                                                qs, qm, ql, dq, pq, last_valid, last_bits);
             const float v = __fmul_rn(score, sc);
             out[t] = v;
             if (use_hist) atomicAdd(hist + (order_key(v) >> 21), 1u);
+#endif
         }
     }
     if (use_hist) {

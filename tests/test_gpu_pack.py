@@ -49,6 +49,64 @@ def test_pack_into_offset_and_errors():
         pk.pack_keys_into(k.transpose(1, 2), packed, token_offset=0)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("offset", [0, 3, 96])
+def test_pack_many_groups_through_c_abi(dtype, offset):
+    """Streaming packer through popkv_pack: more groups than CTAs (the stage ring
+    wraps), a ragged last group, vector and scalar output stores, and 3 heads read
+    with a head stride larger than tokens * head_dim."""
+    import ctypes
+
+    import _native
+
+    lib = _native.c_library()
+    lib.popkv_last_error.restype = ctypes.c_char_p
+    H, T, D = 3, 32 * 700 + 13, 128
+    full = synthetic_keys(H, T + 64, D, seed=11, dtype=dtype).to(DEV)
+    cap = T + offset + 16
+    packed = [torch.zeros(H, cap, D // 32, dtype=dt, device=DEV)
+              for dt in (torch.int32, torch.int32, torch.float16, torch.float16)]
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+    I = ctypes.c_int64
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rc = lib.popkv_pack(ptr(full), code, I(H), I(T), I(D), I((T + 64) * D), *map(ptr, packed),
+                        I(cap), I(offset), None, 0,
+                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, lib.popkv_last_error()
+    torch.cuda.synchronize()
+    ref = O.pack_keys(full[:, :T].float().cpu().numpy(), capacity=cap, token_offset=offset)
+    for name, a, b in zip(("k_sign", "k_mag", "low", "delta"), packed_numpy(packed), ref):
+        np.testing.assert_array_equal(a[:, offset:offset + T], b[:, offset:offset + T], err_msg=name)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_pack_special_values(dtype):
+    """Subnormals, signed zeros, the largest finite values and constant channels:
+    the paired 16-bit comparisons (v+v against max/min) must agree with the oracle's
+    fp32 thresholds."""
+    g = torch.Generator().manual_seed(5)
+    finfo = torch.finfo(dtype)
+    k = torch.randn(2, 96, 64, generator=g)
+    k[:, ::3, 5] = 0.0
+    k[:, 1::3, 5] = -0.0
+    k[:, :, 7] = -0.0                                    # constant -0 channel
+    k[:, :, 9] = 3.0                                     # constant channel
+    k[:, ::2, 11] = finfo.max
+    k[:, 1::2, 11] = -finfo.max
+    k[:, :, 13] = finfo.max / 64 * torch.rand(2, 96, generator=g)
+    sub = finfo.smallest_normal
+    k[:, :, 17] = sub * torch.randint(-8, 9, (2, 96), generator=g) / 8   # subnormals / zeros
+    k[:, :, 19] = sub * (1 + torch.rand(2, 96, generator=g))            # around the smallest normal
+    k[:, :, 23] = -sub * torch.rand(2, 96, generator=g)
+    k = k.to(dtype)
+    got = pk.pack_keys(k.to(DEV), token_capacity=96, with_thresholds=True)
+    torch.cuda.synchronize()
+    (ref, thr) = O.pack_keys(k.float().numpy(), capacity=96, with_thresholds=True)
+    for name, a, b in zip(("k_sign", "k_mag", "low", "delta"), packed_numpy(got[:4]), ref):
+        np.testing.assert_array_equal(a, b, err_msg=name)
+    np.testing.assert_array_equal(got[4].cpu().numpy(), thr)
+
+
 def test_incremental_append_matches_full_pack():
     """build_popkv_cache + append_popkv over 70 tokens equals packing all of them at once."""
     k = synthetic_keys(4, 130, 128, seed=9, dtype=torch.bfloat16).to(DEV)
