@@ -274,6 +274,7 @@ pack_stream_kernel(const __grid_constant__ CUtensorMap key_map, int64_t tokens, 
     constexpr int kBoxElems = 128 / (int)sizeof(T);
     constexpr bool kPaired = sizeof(T) == 2;
     pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // 1024-byte aligned for the swizzled boxes (pointer arithmetic on the shared array
     // keeps the loads in the shared window).
@@ -309,7 +310,6 @@ pack_stream_kernel(const __grid_constant__ CUtensorMap key_map, int64_t tokens, 
         fence_mbar_init();
     }
     __syncthreads();
-    pdl_wait();
     const int64_t first = blockIdx.x, step = gridDim.x;
     if (tid == 0)
         for (int s = 0; s < kPackStages; ++s)
