@@ -268,13 +268,13 @@ pack_stream_kernel(const __grid_constant__ CUtensorMap key_map, int64_t tokens, 
                    int64_t total, int32_t* __restrict__ k_sign, int32_t* __restrict__ k_mag,
                    uint16_t* __restrict__ low, uint16_t* __restrict__ delta, int64_t capacity,
                    int64_t token_offset, float* __restrict__ thresholds, bool ref_div) {
+    pdl_trigger();
+    pdl_wait();
     using S = StreamSmem<T, W>;
     constexpr int D = 32 * W;
     constexpr int kWordBytes = 32 * (int)sizeof(T);
     constexpr int kBoxElems = 128 / (int)sizeof(T);
     constexpr bool kPaired = sizeof(T) == 2;
-    pdl_trigger();
-    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // 1024-byte aligned for the swizzled boxes (pointer arithmetic on the shared array
     // keeps the loads in the shared window).
