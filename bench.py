@@ -161,7 +161,11 @@ def algorithmic_bytes(L, budget, B, kvh, qh, union_rows):
     select = B * qh * L * 4 + B * qh * budget * 4
     attn = 2 * D * 2 * union_rows + B * qh * budget * 4 + 2 * B * qh * D * 2
     append = B * kvh * (32 * D * 2 + 32 * PACKED_BYTES)  # worst case: a full open group
-    return {"score": score, "select": select, "attention": attn, "append": append}
+    # Fused score + select: the packed rows and queries in, the selections out; the
+    # fp32 score round trip of the two-kernel form is gone.
+    score_select = B * kvh * L * PACKED_BYTES + B * qh * D * 2 + B * qh * budget * 4
+    return {"score": score, "select": select, "attention": attn, "append": append,
+            "score_select": score_select}
 
 
 def layer_bytes(B, kvh_local, kv_cap):
@@ -300,6 +304,11 @@ def run_ours(args):
 
     def run_stage(name, i):
         parts = name.split("+")
+        if "scoresel" in parts:
+            pk.score_select(stack.q_in[i], stack.packed[i], head_to_kv=stack.head_to_kv,
+                            budget=budget, tokens=tokens, seq_len=stack.seq_len,
+                            out=stack.indices[i], attn_workspace=stack.workspace[i],
+                            attn_sizes=sizes, scores=stack.scores, hist=stack.score_hist)
         if "score" in parts:
             pk.score(stack.q_in[i], stack.packed[i], head_to_kv=stack.head_to_kv, tokens=tokens,
                      seq_len=stack.seq_len, out=stack.scores, hist=stack.score_hist)
@@ -332,7 +341,10 @@ def run_ours(args):
     # masks its select just wrote: time the prefixes of the layer pipeline and take
     # differences.
     timed = {}
-    for name in ("score+select+attention", "score", "score+select", "append"):
+    names = ["score+select+attention", "score", "score+select", "append"]
+    if stack.fused_select:
+        names = ["scoresel+attention", "scoresel"] + names
+    for name in names:
         for i in range(layers):
             run_stage(name, i)  # eager warm-up of this stage
         if name == "score":
@@ -354,6 +366,9 @@ def run_ours(args):
     stage_ms["select"] = timed["score+select"] - timed["score"]
     stage_ms["attention"] = timed["score+select+attention"] - timed["score+select"]
     stage_ms["append"] = timed["append"]
+    if stack.fused_select:  # the decode step runs the fused kernel
+        stage_ms["score_select"] = timed["scoresel"]
+        stage_ms["attention"] = timed["scoresel+attention"] - timed["scoresel"]
     # The score+select replays left masks set: clear them with one attention pass.
     for i in range(layers):
         run_stage("attention", i)
@@ -381,7 +396,11 @@ def run_ours(args):
                   "gbs": nbytes[n] / (stage_ms[n] * 1e-3) / 1e9,
                   "frac": nbytes[n] / (stage_ms[n] * 1e-3) / 1e9 / hbm} for n in stage_ms}
     stages["pack"]["note"] = "one-time prefill pack per layer (all sequences), L2 flushed, not in value"
-    dominant = max(("score", "select", "attention"), key=lambda n: stage_ms[n])
+    in_step = ("score_select", "attention") if stack.fused_select else ("score", "select", "attention")
+    if stack.fused_select:
+        for n in ("score", "select"):
+            stages[n]["note"] = "two-kernel form, not in the decode step (the fused score_select runs)"
+    dominant = max(in_step, key=lambda n: stage_ms[n])
     traffic = None  # DRAM bytes per launch from the committed ncu summary of this workload
     try:
         for ln in (ROOT / "profiles" / "roofline_traffic_configs1.txt").read_text().splitlines():
@@ -390,7 +409,7 @@ def run_ours(args):
                 traffic = float(val)
     except Exception:
         traffic = None
-    step_bytes = sum(nbytes[n] for n in ("score", "select", "attention", "append"))
+    step_bytes = sum(nbytes[n] for n in in_step + ("append",))
 
     # ---- e2e: public API with pinned host inputs and outputs, copies inside the region.
     host_q = [qs[s].cpu().pin_memory() for s in range(total_steps)]

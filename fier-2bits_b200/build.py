@@ -50,14 +50,14 @@ def _run(cmd, verbose):
 
 
 def build_c_library(force: bool = False, verbose: bool = False) -> Path:
-    deps = [CSRC / s for s in CUDA_SOURCES] + [CSRC / "common.cuh", INCLUDE / "popkv_b200.h"]
+    deps = [CSRC / s for s in CUDA_SOURCES] + [CSRC / "common.cuh", CSRC / "score_core.cuh", INCLUDE / "popkv_b200.h"]
     if not force and not _stale(C_LIB, deps):
         return C_LIB
     LIB.mkdir(exist_ok=True)
     obj_dir = LIB / "obj"
     obj_dir.mkdir(exist_ok=True)
     objs, jobs = [], []
-    headers = [CSRC / "common.cuh", INCLUDE / "popkv_b200.h"]
+    headers = [CSRC / "common.cuh", CSRC / "score_core.cuh", INCLUDE / "popkv_b200.h"]
     for src in CUDA_SOURCES:
         obj = obj_dir / (Path(src).stem + ".o")
         objs.append(obj)

@@ -25,9 +25,10 @@
 // buffer holds (heavy ties), the radix select and ranking run over the whole row
 // instead: slower, same result.  Optionally the selection is also OR-ed into the
 // per-KV-head token bitmask the fused attention consumes.  No CTA waits on another.
+#include <cmath>
 #include <cooperative_groups.h>
 
-#include "common.cuh"
+#include "score_core.cuh"
 
 namespace popkv {
 namespace {
@@ -674,8 +675,95 @@ __device__ void cluster_find_bin(RowShared& sh, int slot, int nbins, uint32_t re
     __syncthreads();
 }
 
-template <int C, int NT>
-__global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(SelectArgs a, int per) {
+// Inputs of the fused score + select path: the packed cache and the queries, scored
+// inside select_row_kernel instead of read back from a score buffer.
+struct ScoreIn {
+    const void* queries;
+    int q_heads, D;
+    const int32_t* k_sign;
+    const int32_t* k_mag;
+    const uint16_t* k_low;
+    const uint16_t* k_delta;
+    int kv_heads;
+    int64_t capacity;
+    bool per_batch;
+    const int64_t* head_to_kv;
+    float scale;
+    bool ref_div, vec;
+};
+
+// Scores of this CTA's slice [lo, lo + n) of row `row` (query head row % QH of
+// sequence row / QH) into s_keys as order keys, counted into sh.hist[0] by their top
+// 11 bits.  Bit-identical to score_kernel: the same packed-row loads, query packing
+// and token_score arithmetic.  Every thread calls it; it ends with a barrier.
+template <typename TQ, int W, int NT>
+__device__ void score_slice(const SelectArgs& a, const ScoreIn& in, int64_t row, int64_t lo, int n,
+                            uint32_t* s_keys, RowShared& sh) {
+    __shared__ float s_abs[W * 33];
+    __shared__ uint32_t s_qs[W], s_qm[W];
+    __shared__ float s_ql[W], s_qd[W];
+    __shared__ int s_head;
+    const int tid = threadIdx.x;
+    const int64_t b = row / a.rows_per_seq;
+    const int qh = static_cast<int>(row - b * a.rows_per_seq);
+    if (tid < 32) {
+        if (tid == 0) s_head = qh;
+        __syncwarp();
+        pack_query_heads<TQ, W, 1>(static_cast<const TQ*>(in.queries), b, in.q_heads, in.D, &s_head, 1,
+                                   s_abs, s_qs, s_qm, s_ql, s_qd, in.ref_div);
+    }
+    const int64_t kvh = in.head_to_kv[qh];
+    const int64_t cache_head = (in.per_batch ? b * in.kv_heads : 0) + kvh;
+    const int64_t base = cache_head * in.capacity + lo;
+    __syncthreads();
+    constexpr bool kFull = true;  // W * 32 == D on this path
+    uint32_t qs[W], qm[W];
+    float ql[W], dq[W];
+    int pq[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+        qs[w] = s_qs[w];
+        qm[w] = s_qm[w];
+        ql[w] = s_ql[w];
+        dq[w] = s_qd[w];
+        pq[w] = __popc(qm[w]);
+    }
+    const float sc = in.ref_div ? rsqrtf(static_cast<float>(in.D)) : in.scale;
+    auto one = [&](const PackedRow<W, true>& r) {
+        float klf[W], kdf[W];
+        half_words<W>(r.l, klf);
+        half_words<W>(r.d, kdf);
+        const uint32_t pkm = mag_popcounts<W>(r.m, 0xffffffffu);
+        const float score = token_score<W, kFull>(r.s, r.m, klf, kdf, pkm, qs, qm, ql, dq, pq,
+                                                  0xffffffffu, 32);
+        return order_key(__fmul_rn(score, sc));
+    };
+    int i = tid;
+    for (; i + NT < n; i += 2 * NT) {
+        PackedRow<W, true> r0, r1;
+        r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i) * W);
+        r1.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i + NT) * W);
+        const uint32_t k0 = one(r0), k1 = one(r1);
+        s_keys[i] = k0;
+        s_keys[i + NT] = k1;
+        atomicAdd(&sh.hist[0][hidx(k0 >> 21)], 1u);
+        atomicAdd(&sh.hist[0][hidx(k1 >> 21)], 1u);
+    }
+    if (i < n) {
+        PackedRow<W, true> r0;
+        r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i) * W);
+        const uint32_t k0 = one(r0);
+        s_keys[i] = k0;
+        atomicAdd(&sh.hist[0][hidx(k0 >> 21)], 1u);
+    }
+    __syncthreads();
+}
+
+// FUSE_W == 0: keys from the score buffer (and the scorer's histogram when given).
+// FUSE_W > 0: the slice is scored here (score_slice, head_dim = 32 * FUSE_W, queries
+// of type TQ) and no score buffer or histogram workspace is used.
+template <int C, int NT, int FUSE_W = 0, typename TQ = float>
+__global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(SelectArgs a, int per, ScoreIn in) {
     pdl_trigger();
     pdl_wait();
     __shared__ __align__(16) RowShared sh;
@@ -709,10 +797,24 @@ __global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(Select
                 if (r.mask_words) atomicOr(r.mask_words + (t >> 1), r.bit << ((t & 1) * 16));
             }
         if constexpr (C > 1) { cluster_arrive(); cluster_wait(); }  // every CTA has read the histogram
-        if (crank == 0)
+        if (crank == 0 && a.hist != nullptr)
             for (int i = tid; i < kBins; i += NT) hrow[i] = 0u;
         return;
     }
+    uint32_t remaining = static_cast<uint32_t>(k);
+    const int first = tid * per;
+    const int nvalid = n - first <= 0 ? 0 : (n - first < per ? n - first : per);
+    const uint32_t* mine = s_keys + first;
+    if constexpr (FUSE_W > 0) {
+        for (int i = tid; i < kPaddedBins; i += NT) {
+            sh.hist[0][i] = 0u;
+            sh.hist[1][i] = 0u;
+            sh.hist[2][i] = 0u;
+        }
+        __syncthreads();
+        score_slice<TQ, FUSE_W, NT>(a, in, row, lo, n, s_keys, sh);
+        cluster_find_bin<C>(sh, 0, kBins, remaining);
+    } else {
 
     // 1. The slice's scores into shared memory by one bulk copy (the TMA engine
     // streams it while the threads set up the histograms), then turned into order
@@ -752,9 +854,6 @@ __global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(Select
         reinterpret_cast<uint4*>(s_keys)[i] = v;
     }
     for (int i = (n4 << 2) + tid; i < n; i += NT) s_keys[i] = order_key(__ldg(src + i));
-    const int first = tid * per;
-    const int nvalid = n - first <= 0 ? 0 : (n - first < per ? n - first : per);
-    const uint32_t* mine = s_keys + first;
     __syncthreads();
 
     // 2. Top digit: the scorer's histogram when it counted this row's L scores (the
@@ -767,7 +866,6 @@ __global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(Select
         if (lane == 0) sh.count = local;
     }
     __syncthreads();
-    uint32_t remaining = static_cast<uint32_t>(k);
     if (sh.count == static_cast<uint32_t>(L)) {
         cluster_find_bin<1>(sh, 0, kBins, remaining);  // local: every CTA holds the totals
     } else {
@@ -780,6 +878,7 @@ __global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(Select
         }
         cluster_find_bin<C>(sh, 0, kBins, remaining);
     }
+    }  // FUSE_W == 0
     uint32_t prefix = sh.sel_bin << 21;
     remaining -= sh.sel_above;
 
@@ -808,7 +907,7 @@ __global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(Select
     const uint64_t bin_bits = (static_cast<uint64_t>(bin_w[1]) << 32) | bin_w[0];
     cluster_find_bin<C>(sh, 1, kBins, remaining);
     // Every CTA of the cluster has now read the scorer's histogram: zero it for the next step.
-    if (crank == 0)
+    if (crank == 0 && a.hist != nullptr)
         for (int i = tid; i < kBins; i += NT) hrow[i] = 0u;
     const uint32_t d2 = sh.sel_bin;
     prefix |= d2 << 10;
@@ -985,7 +1084,7 @@ extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_str
                 cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_keys);
                 if (C > 1) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
                 launch_pdl_cluster(kern, dim3((unsigned)C, (unsigned)rows), dim3(NT), smem_keys,
-                                   st, (unsigned)C, a, per);
+                                   st, (unsigned)C, a, per, ScoreIn{});
             };
             if (NT == kRowThreads) {
                 switch (C) {
@@ -1017,4 +1116,99 @@ extern "C" int popkv_select(const float* scores, int64_t rows, int64_t score_str
     cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_pdl(select_kernel, dim3((unsigned)rows), dim3(kRowThreads), smem, st, a);
     return check_launch("popkv_select");
+}
+
+extern "C" int popkv_score_select(const void* queries, int q_dtype, int64_t batch, int64_t q_heads,
+                                  int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                                  const uint16_t* low, const uint16_t* delta, int64_t kv_heads,
+                                  int64_t capacity, int cache_per_batch, const int64_t* head_to_kv,
+                                  int64_t tokens, const int32_t* seq_len, int64_t budget,
+                                  int32_t* indices, uint16_t* head_masks, int64_t mask_stride,
+                                  int64_t heads_per_kv, float* scores, int64_t score_stride,
+                                  void* select_workspace, size_t select_workspace_bytes, int flags,
+                                  popkv_stream_t stream) {
+    if (batch < 0 || q_heads <= 0 || head_dim <= 0 || kv_heads <= 0)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "queries must be [batch, q_heads, head_dim]");
+    if (tokens <= 0 || tokens > capacity)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "invalid score token count %lld (capacity %lld)",
+                    (long long)tokens, (long long)capacity);
+    if (budget <= 1)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "budget must reserve at least one retrieved and one current token");
+    if (head_masks != nullptr) {
+        if (heads_per_kv <= 0 || heads_per_kv > 16 || q_heads % heads_per_kv != 0)
+            return fail(POPKV_ERR_INVALID_ARGUMENT, "head masks need 0 < heads_per_kv <= 16 dividing q_heads");
+        if (mask_stride < tokens + 1 || mask_stride % 2 != 0 || !aligned(head_masks, 4))
+            return fail(POPKV_ERR_INVALID_ARGUMENT, "mask_stride must be even and >= tokens + 1");
+    }
+    if (batch == 0) return POPKV_OK;
+    if (!queries || !k_sign || !k_mag || !low || !delta || !head_to_kv || !indices)
+        return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
+    const int64_t rows = batch * q_heads;
+    // The fused kernel: head_dim 128, 16-bit queries, rows that fit one cluster.
+    int C = 1;
+    while (C < 8 && (tokens + C - 1) / C > (int64_t)kRowThreads * kRowMaxPer) C *= 2;
+    while (C < 8 && rows * C * 2 <= num_sms() && (tokens + 2 * C - 1) / (2 * C) >= 2048) C *= 2;
+    int NT = kRowThreads;
+    if (rows * C > 2 * (int64_t)num_sms()) {
+        int C2 = 1;
+        while (C2 < 8 && (tokens + C2 - 1) / C2 > (int64_t)(kRowThreads / 2) * kRowMaxPer) C2 *= 2;
+        if ((tokens + C2 - 1) / C2 <= (int64_t)(kRowThreads / 2) * kRowMaxPer) { C = C2; NT = kRowThreads / 2; }
+    }
+    const int64_t chunk = ((tokens + C - 1) / C + 3) / 4 * 4;
+    const bool vec = aligned(k_sign, 16) && aligned(k_mag, 16) && aligned(low, 8) && aligned(delta, 8);
+    const bool fused = head_dim == 128 && (q_dtype == POPKV_BF16 || q_dtype == POPKV_F16) && vec &&
+                       chunk <= (int64_t)NT * kRowMaxPer && rows <= 65535 &&
+                       (flags & POPKV_FLAG_UNFUSED_SELECT) == 0;
+    if (!fused) {
+        if (!scores || !select_workspace)
+            return fail(POPKV_ERR_UNSUPPORTED,
+                        "these sizes need the two-kernel path: pass a score buffer and a select workspace");
+        int rc = popkv_score(queries, q_dtype, batch, q_heads, head_dim, k_sign, k_mag, low, delta,
+                             kv_heads, capacity, cache_per_batch, head_to_kv, tokens, seq_len, scores,
+                             score_stride, select_workspace, flags, stream);
+        if (rc != POPKV_OK) return rc;
+        return popkv_select(scores, rows, score_stride, tokens, seq_len, q_heads, budget, indices,
+                            head_masks, mask_stride, heads_per_kv, select_workspace,
+                            select_workspace_bytes, stream);
+    }
+    SelectArgs a = {};
+    a.tokens = tokens; a.seq_len = seq_len; a.rows_per_seq = q_heads;
+    a.budget = budget; a.indices = indices; a.masks = head_masks; a.mask_stride = mask_stride;
+    a.heads_per_kv = (int)(heads_per_kv > 0 ? heads_per_kv : 1);
+    ScoreIn in = {};
+    in.queries = queries; in.q_heads = (int)q_heads; in.D = (int)head_dim;
+    in.k_sign = k_sign; in.k_mag = k_mag; in.k_low = low; in.k_delta = delta;
+    in.kv_heads = (int)kv_heads; in.capacity = capacity; in.per_batch = cache_per_batch != 0;
+    in.head_to_kv = head_to_kv; in.scale = (float)(1.0 / std::sqrt((double)head_dim));
+    in.ref_div = (flags & POPKV_FLAG_REFERENCE_DIVISION) != 0; in.vec = vec;
+    const int per = (int)((chunk + NT - 1) / NT) | 1;  // odd
+    const size_t smem_keys = (size_t)per * NT * 4;
+    const cudaStream_t st = as_stream(stream);
+    auto go = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_keys);
+        if (C > 1) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        launch_pdl_cluster(kern, dim3((unsigned)C, (unsigned)rows), dim3(NT), smem_keys, st,
+                           (unsigned)C, a, per, in);
+    };
+    auto by_c = [&](auto tq) {
+        using TQ = decltype(tq);
+        if (NT == kRowThreads) {
+            switch (C) {
+                case 1: go(select_row_kernel<1, kRowThreads, 4, TQ>); break;
+                case 2: go(select_row_kernel<2, kRowThreads, 4, TQ>); break;
+                case 4: go(select_row_kernel<4, kRowThreads, 4, TQ>); break;
+                default: go(select_row_kernel<8, kRowThreads, 4, TQ>); break;
+            }
+        } else {
+            switch (C) {
+                case 1: go(select_row_kernel<1, kRowThreads / 2, 4, TQ>); break;
+                case 2: go(select_row_kernel<2, kRowThreads / 2, 4, TQ>); break;
+                case 4: go(select_row_kernel<4, kRowThreads / 2, 4, TQ>); break;
+                default: go(select_row_kernel<8, kRowThreads / 2, 4, TQ>); break;
+            }
+        }
+    };
+    if (q_dtype == POPKV_BF16) by_c(__nv_bfloat16{});
+    else by_c(__half{});
+    return check_launch("popkv_score_select");
 }

@@ -233,6 +233,74 @@ at::Tensor select_topk(const at::Tensor& scores, int64_t budget, int64_t tokens,
     return idx;
 }
 
+// Score + select in one call (popkv_score_select): indices [B*QH, budget], optionally
+// the attention workspace's head bitmask; `scores`/`hist` serve the two-kernel
+// fallback only.
+at::Tensor score_select(const at::Tensor& queries, const at::Tensor& k_sign, const at::Tensor& k_mag,
+                        const at::Tensor& low, const at::Tensor& delta, const at::Tensor& head_to_kv,
+                        int64_t budget, int64_t tokens, int64_t flags,
+                        const c10::optional<at::Tensor>& seq_len, const c10::optional<at::Tensor>& out,
+                        const c10::optional<at::Tensor>& attn_workspace, std::vector<int64_t> attn_sizes,
+                        const c10::optional<at::Tensor>& scores, const c10::optional<at::Tensor>& hist) {
+    CHECK_CUDA(queries); CHECK_CONTIGUOUS(queries);
+    TORCH_CHECK(queries.dim() == 3, "queries must be [B, QH, D]");
+    check_packed({k_sign, k_mag, low, delta});
+    CHECK_CUDA(head_to_kv); CHECK_CONTIGUOUS(head_to_kv);
+    TORCH_CHECK(head_to_kv.scalar_type() == at::kLong, "head mapping must be int64");
+    TORCH_CHECK(head_to_kv.numel() == queries.size(1), "head mapping needs one entry per query head");
+    const int64_t batch = queries.size(0), q_heads = queries.size(1), dim = queries.size(2);
+    const bool per_batch = k_sign.dim() == 4;
+    if (per_batch) TORCH_CHECK(k_sign.size(0) == batch, "batched packed cache must match the batch");
+    const int64_t kv_heads = per_batch ? k_sign.size(1) : k_sign.size(0);
+    const int64_t cap = k_sign.size(-2);
+    TORCH_CHECK(k_sign.size(-1) == (dim + 31) / 32, "packed words do not match head_dim");
+    TORCH_CHECK(tokens > 0 && tokens <= cap, "invalid score token count");
+    const int32_t* sl = nullptr;
+    if (seq_len) { CHECK_CUDA(*seq_len); CHECK_DTYPE(*seq_len, at::kInt); sl = seq_len->data_ptr<int32_t>(); }
+    c10::cuda::CUDAGuard guard(queries.device());
+    const int64_t rows = batch * q_heads;
+    at::Tensor idx;
+    if (out) {
+        idx = *out;
+        CHECK_CUDA(idx); CHECK_CONTIGUOUS(idx); CHECK_DTYPE(idx, at::kInt);
+        TORCH_CHECK(idx.numel() == rows * budget, "indices out must hold rows x budget entries");
+    } else {
+        idx = at::empty({rows, budget}, queries.options().dtype(at::kInt));
+    }
+    uint16_t* masks = nullptr;
+    int64_t mask_stride = 0, heads_per_kv = 0;
+    if (attn_workspace) {
+        TORCH_CHECK(attn_sizes.size() == 6, "attn_sizes = (batch, q_heads, kv_heads, head_dim, tokens, splits)");
+        CHECK_CUDA(*attn_workspace); CHECK_CONTIGUOUS(*attn_workspace);
+        const size_t need = popkv_sparse_attention_workspace_bytes(attn_sizes[0], attn_sizes[1], attn_sizes[2],
+                                                                   attn_sizes[3], attn_sizes[4], attn_sizes[5]);
+        TORCH_CHECK((size_t)attn_workspace->nbytes() >= need, "attention workspace too small");
+        check_status(popkv_sparse_attention_masks(attn_workspace->data_ptr(), attn_sizes[0], attn_sizes[1],
+                                                  attn_sizes[2], attn_sizes[3], attn_sizes[4], attn_sizes[5],
+                                                  &masks, &mask_stride),
+                     "popkv_sparse_attention_masks");
+        heads_per_kv = attn_sizes[1] / attn_sizes[2];
+        TORCH_CHECK(q_heads == attn_sizes[1], "attention sizes must match the queries");
+    }
+    float* sp = nullptr;
+    int64_t sstride = tokens;
+    if (scores) {
+        CHECK_CUDA(*scores); CHECK_CONTIGUOUS(*scores); CHECK_DTYPE(*scores, at::kFloat);
+        TORCH_CHECK(scores->numel() >= rows * tokens && scores->numel() % rows == 0, "scores buffer too small");
+        sp = scores->data_ptr<float>();
+        sstride = scores->numel() / rows;
+    }
+    const int rc = popkv_score_select(
+        queries.data_ptr(), dtype_code(queries), batch, q_heads, dim, k_sign.data_ptr<int32_t>(),
+        k_mag.data_ptr<int32_t>(), reinterpret_cast<const uint16_t*>(low.data_ptr<at::Half>()),
+        reinterpret_cast<const uint16_t*>(delta.data_ptr<at::Half>()), kv_heads, cap, per_batch ? 1 : 0,
+        head_to_kv.data_ptr<int64_t>(), tokens, sl, budget, idx.data_ptr<int32_t>(), masks, mask_stride,
+        heads_per_kv, sp, sstride, select_ws_ptr(hist, rows, tokens), hist ? (size_t)hist->nbytes() : 0,
+        (int)flags, stream_of(queries));
+    check_status(rc, "popkv_score_select");
+    return idx;
+}
+
 std::mutex g_ws_mutex;
 std::map<std::vector<int64_t>, at::Tensor> g_workspaces;
 
@@ -478,6 +546,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("seq_len") = py::none(), py::arg("rows_per_seq") = 0, py::arg("out") = py::none(),
           py::arg("attn_workspace") = py::none(), py::arg("attn_sizes") = std::vector<int64_t>{},
           py::arg("hist") = py::none());
+    m.def("score_select", &score_select, py::arg("queries"), py::arg("k_sign"), py::arg("k_mag"),
+          py::arg("low"), py::arg("delta"), py::arg("head_to_kv"), py::arg("budget"), py::arg("tokens"),
+          py::arg("flags"), py::arg("seq_len"), py::arg("out"), py::arg("attn_workspace"),
+          py::arg("attn_sizes"), py::arg("scores"), py::arg("hist"));
     m.def("sparse_attention_premasked", &sparse_attention_premasked, py::arg("queries"), py::arg("key_cache"),
           py::arg("value_cache"), py::arg("tokens"), py::arg("current_keys"), py::arg("current_values"),
           py::arg("seq_len"), py::arg("workspace"), py::arg("splits"), py::arg("out"),

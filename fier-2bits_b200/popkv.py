@@ -18,6 +18,7 @@ computes on the CPU.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -342,8 +343,13 @@ class RetrievalStack:
     def __init__(self, *, layers: int, batch: int, kv_heads: int, q_heads: int, head_dim: int,
                  max_tokens: int, budget: int, dtype=torch.bfloat16, device=None,
                  process_group=None, gather_wait: str | None = None,
-                 dense_layers: tuple[int, ...] = ()):
+                 dense_layers: tuple[int, ...] = (), fused_select: bool | None = None):
         self.device = torch.device(device or "cuda")
+        # Score and select in one kernel (default; POPKV_FUSED_SELECT=0 or
+        # fused_select=False keeps the scorer and the select as two kernels).
+        if fused_select is None:
+            fused_select = os.environ.get("POPKV_FUSED_SELECT", "1") != "0"
+        self.fused_select = bool(fused_select)
         # Layers attended densely (the reference's full_layers, popkv.py:542-551):
         # no score/select, attention over every cached token plus the current one.
         self.dense_layers = frozenset(int(i) for i in dense_layers)
@@ -392,7 +398,6 @@ class RetrievalStack:
         # for its own rows (what a decoder whose next layer reads them needs).
         self.peer = None
         self._gathered = None
-        import os
         self.gather_wait = gather_wait or os.environ.get("POPKV_GATHER_WAIT", "step")
         if self.gather_wait not in ("step", "layer"):
             raise ValueError("gather_wait is 'step' or 'layer'")
@@ -472,17 +477,19 @@ class RetrievalStack:
             if self.world > 1:
                 raise RuntimeError("dense layers are not sharded")
             return
-        pk.score(self.q_in[i], self.packed[i], head_to_kv=self.head_to_kv, tokens=tokens,
-                 seq_len=self.seq_len, out=self.scores, hist=self.score_hist)
+        sizes = (self.batch, self.q_heads, self.kv_heads, self.head_dim, tokens, 0)
+        # Score + select in one launch (the score buffer and histogram workspace serve
+        # the two-kernel form, for sizes the fused kernel does not take).
+        pk.score_select(self.q_in[i], self.packed[i], head_to_kv=self.head_to_kv,
+                        budget=self.budget, tokens=tokens, seq_len=self.seq_len,
+                        out=self.indices[i], attn_workspace=self.workspace[i], attn_sizes=sizes,
+                        scores=self.scores, hist=self.score_hist,
+                        flags=0 if self.fused_select else pk.UNFUSED_SELECT)
         self.side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.side):
             pk.append_keys(self.key_cache[i], self.value_cache[i], self.k_in[i], self.v_in[i],
                            self.packed[i], position=0, seq_len=self.seq_len,
                            kv_heads_per_seq=self.kv_heads)
-        sizes = (self.batch, self.q_heads, self.kv_heads, self.head_dim, tokens, 0)
-        pk.select(self.scores.view(-1, self.capacity), budget=self.budget, tokens=tokens,
-                  seq_len=self.seq_len, rows_per_seq=self.q_heads, out=self.indices[i],
-                  attn_workspace=self.workspace[i], attn_sizes=sizes, hist=self.score_hist)
         push = self.peer is not None and self.gather_wait == "step"
         pk.sparse_attention_premasked(self.q_in[i], self.key_cache[i], self.value_cache[i],
                                       tokens=tokens, current_keys=self.k_in[i],

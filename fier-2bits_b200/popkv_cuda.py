@@ -26,6 +26,8 @@ from _native import extension
 
 # Flag: divide like a --use_fast_math build of the reference extension (see the C header).
 REFERENCE_DIVISION = 1
+# Flag: score_select takes the two-kernel path (score buffer + select).
+UNFUSED_SELECT = 2
 
 
 def _packed(packed) -> Sequence[torch.Tensor]:
@@ -105,6 +107,27 @@ def select(scores: torch.Tensor, *, budget: int, tokens: int | None = None,
     tokens = int(scores.shape[-1]) if tokens is None else int(tokens)
     return extension().select(scores, int(budget), tokens, seq_len, int(rows_per_seq), out,
                               attn_workspace, [int(x) for x in attn_sizes], hist)
+
+
+def score_select(queries: torch.Tensor, packed, *, head_to_kv: torch.Tensor, budget: int,
+                 tokens: int, seq_len: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 attn_workspace: torch.Tensor | None = None, attn_sizes: tuple = (),
+                 scores: torch.Tensor | None = None, hist: torch.Tensor | None = None,
+                 flags: int = 0) -> torch.Tensor:
+    """``select(score(queries, packed))`` in one launch: int32 [B*QH, budget].
+
+    Identical indices (and head bitmask with ``attn_workspace``) to the two calls.
+    With head_dim 128 and bf16/fp16 queries no score buffer is written; other sizes
+    fall back to score + select and need ``scores`` ([B*QH, >= tokens] fp32) and
+    ``hist`` (a select workspace).
+    """
+    if queries.ndim != 3 or not queries.is_cuda or not queries.is_contiguous():
+        raise ValueError("queries must be contiguous CUDA [batch, query heads, head dim]")
+    if int(budget) <= 1:
+        raise ValueError("budget must reserve at least one retrieved and one current token")
+    return extension().score_select(queries, *_packed(packed), head_to_kv.contiguous(), int(budget),
+                                    int(tokens), int(flags), seq_len, out, attn_workspace,
+                                    [int(x) for x in attn_sizes], scores, hist)
 
 
 def sparse_attention_premasked(queries, key_cache, value_cache, *, tokens: int, current_keys,

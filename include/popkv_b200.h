@@ -52,7 +52,10 @@ enum popkv_flags {
      * scale scores by rsqrtf(D), as a --use_fast_math build of the reference
      * extension does (popkv_cuda.py:20).  Default: IEEE division, 1/sqrt(D)
      * correctly rounded on the host. */
-    POPKV_FLAG_REFERENCE_DIVISION = 1
+    POPKV_FLAG_REFERENCE_DIVISION = 1,
+    /* popkv_score_select: take the two-kernel path (score buffer + select) even where
+     * the fused kernel applies. */
+    POPKV_FLAG_UNFUSED_SELECT = 2
 };
 
 /* Static description of an error code. */
@@ -141,6 +144,30 @@ int popkv_select(const float* scores, int64_t rows, int64_t score_stride, int64_
                  int32_t* indices, uint16_t* head_masks, int64_t mask_stride,
                  int64_t heads_per_kv, void* select_workspace, size_t select_workspace_bytes,
                  popkv_stream_t stream);
+
+/*
+ * (c)+(d)+(e) fused: score and select in one launch.  Replaces the pair
+ * popkv_score_cuda + torch.topk/_append_current of one decode step
+ * (popkv.py:587-600, csrc/popkv_ext.cu:229-254).
+ *
+ * Arguments as popkv_score (queries, packed cache, head_to_kv, tokens, seq_len,
+ * flags) and popkv_select (budget, indices, head_masks, mask_stride, heads_per_kv)
+ * with rows = batch*q_heads, rows_per_seq = q_heads.  The indices (and head masks)
+ * are identical to popkv_score followed by popkv_select.
+ * With head_dim 128, bf16/fp16 queries and 16-byte aligned packed words, one
+ * cluster of CTAs per row scores its slices into shared memory and selects from
+ * there: no score buffer, no histogram workspace; scores / select_workspace may
+ * then be NULL and are not touched.  Other sizes (or POPKV_FLAG_UNFUSED_SELECT)
+ * run popkv_score + popkv_select and need both (POPKV_ERR_UNSUPPORTED without).
+ */
+int popkv_score_select(const void* queries, int q_dtype, int64_t batch, int64_t q_heads,
+                       int64_t head_dim, const int32_t* k_sign, const int32_t* k_mag,
+                       const uint16_t* low, const uint16_t* delta, int64_t kv_heads,
+                       int64_t capacity, int cache_per_batch, const int64_t* head_to_kv,
+                       int64_t tokens, const int32_t* seq_len, int64_t budget, int32_t* indices,
+                       uint16_t* head_masks, int64_t mask_stride, int64_t heads_per_kv,
+                       float* scores, int64_t score_stride, void* select_workspace,
+                       size_t select_workspace_bytes, int flags, popkv_stream_t stream);
 
 /*
  * (f) Fused gather + exact split-K decode attention.  Replaces gather_selected_kv +

@@ -22,11 +22,13 @@ pytestmark = pytest.mark.gpu
 KVH, QH, D, L0, BUDGET = 8, 32, 128, 32768, 4096
 
 
-def test_configs1_stack_matches_oracle():
+@pytest.mark.parametrize("fused", [True, False])
+def test_configs1_stack_matches_oracle(fused):
     layers, steps = 2, 3
     dev = torch.device("cuda")
     stack = popkv.RetrievalStack(layers=layers, batch=1, kv_heads=KVH, q_heads=QH, head_dim=D,
-                                 max_tokens=L0 + 16, budget=BUDGET, dtype=torch.bfloat16, device=dev)
+                                 max_tokens=L0 + 16, budget=BUDGET, dtype=torch.bfloat16, device=dev,
+                                 fused_select=fused)
     gens = []
     for i in range(layers):
         syn = SyntheticLayer(kv_heads=KVH, q_heads=QH, head_dim=D, seed=1000 + i, device=dev)
