@@ -706,15 +706,27 @@ __device__ void score_slice(const SelectArgs& a, const ScoreIn& in, int64_t row,
     const int tid = threadIdx.x;
     const int64_t b = row / a.rows_per_seq;
     const int qh = static_cast<int>(row - b * a.rows_per_seq);
+    const int64_t kvh = in.head_to_kv[qh];
+    const int64_t cache_head = (in.per_batch ? b * in.kv_heads : 0) + kvh;
+    const int64_t base = cache_head * in.capacity + lo;
+    // The slice's packed rows towards L2 in four bulk prefetches, and this thread's
+    // first two rows into registers, all before the query pack.
+    if (tid == 32 && n >= 4) {
+        const uint32_t wb = static_cast<uint32_t>(n) * W * 4u & ~15u, hb = static_cast<uint32_t>(n) * W * 2u & ~15u;
+        prefetch_l2(in.k_sign + base * W, wb);
+        prefetch_l2(in.k_mag + base * W, wb);
+        prefetch_l2(in.k_low + base * W, hb);
+        prefetch_l2(in.k_delta + base * W, hb);
+    }
+    PackedRow<W, true> r0, r1;
+    if (tid < n) r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + tid) * W);
+    if (tid + NT < n) r1.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + tid + NT) * W);
     if (tid < 32) {
         if (tid == 0) s_head = qh;
         __syncwarp();
         pack_query_heads<TQ, W, 1>(static_cast<const TQ*>(in.queries), b, in.q_heads, in.D, &s_head, 1,
                                    s_abs, s_qs, s_qm, s_ql, s_qd, in.ref_div);
     }
-    const int64_t kvh = in.head_to_kv[qh];
-    const int64_t cache_head = (in.per_batch ? b * in.kv_heads : 0) + kvh;
-    const int64_t base = cache_head * in.capacity + lo;
     __syncthreads();
     constexpr bool kFull = true;  // W * 32 == D on this path
     uint32_t qs[W], qm[W];
@@ -738,25 +750,37 @@ __device__ void score_slice(const SelectArgs& a, const ScoreIn& in, int64_t row,
                                                   0xffffffffu, 32);
         return order_key(__fmul_rn(score, sc));
     };
+    // With 512-thread CTAs (two per SM, long rows) odd lanes count into a second copy
+    // of the top-digit histogram (fewer lanes of a warp on one address); the copies
+    // are added after the slice.  (Measured: helps there, not with 1024 threads.)
+    constexpr bool kTwoCopies = NT < kRowThreads;
+    uint32_t* hist0 = (kTwoCopies && (threadIdx.x & 1)) ? sh.hist[1] : sh.hist[0];
     int i = tid;
     for (; i + NT < n; i += 2 * NT) {
-        PackedRow<W, true> r0, r1;
-        r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i) * W);
-        r1.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i + NT) * W);
+        if (i != tid) {
+            r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i) * W);
+            r1.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i + NT) * W);
+        }
         const uint32_t k0 = one(r0), k1 = one(r1);
         s_keys[i] = k0;
         s_keys[i + NT] = k1;
-        atomicAdd(&sh.hist[0][hidx(k0 >> 21)], 1u);
-        atomicAdd(&sh.hist[0][hidx(k1 >> 21)], 1u);
+        atomicAdd(&hist0[hidx(k0 >> 21)], 1u);
+        atomicAdd(&hist0[hidx(k1 >> 21)], 1u);
     }
     if (i < n) {
-        PackedRow<W, true> r0;
-        r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i) * W);
+        if (i != tid) r0.load(in.k_sign, in.k_mag, in.k_low, in.k_delta, (base + i) * W);
         const uint32_t k0 = one(r0);
         s_keys[i] = k0;
-        atomicAdd(&sh.hist[0][hidx(k0 >> 21)], 1u);
+        atomicAdd(&hist0[hidx(k0 >> 21)], 1u);
     }
     __syncthreads();
+    if constexpr (kTwoCopies) {
+        for (int j = tid; j < kPaddedBins; j += NT) {
+            sh.hist[0][j] += sh.hist[1][j];
+            sh.hist[1][j] = 0u;
+        }
+        __syncthreads();
+    }
 }
 
 // FUSE_W == 0: keys from the score buffer (and the scorer's histogram when given).
