@@ -210,6 +210,12 @@ def run_ours(args):
                                  dtype=torch.bfloat16, device=dev, process_group=group)
     (k0, k1), (q0, q1) = stack.kv_range, stack.q_range
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2x L2
+    # One untimed pack first: the kernel's module load and launch set-up stay out of
+    # the timed prefill packs.
+    warm = torch.zeros(k1 - k0, 64, D, dtype=torch.bfloat16, device=dev)
+    pk.pack_keys(warm, token_capacity=64)
+    torch.cuda.synchronize()
+    del warm
     pack_ms = 0.0
     gens = []
     for i in range(layers):
@@ -595,6 +601,11 @@ def decoder_stage_times(dec, budget, hbm, reps=10):
 
     def run(name):
         for i in sparse:
+            if "fused" in name:
+                pk.score_select(st.q_in[i], st.packed[i], head_to_kv=st.head_to_kv, budget=budget,
+                                tokens=tokens, seq_len=st.seq_len, out=st.indices[i],
+                                attn_workspace=st.workspace[i], attn_sizes=sizes,
+                                scores=st.scores, hist=st.score_hist)
             if "score" in name:
                 pk.score(st.q_in[i], st.packed[i], head_to_kv=st.head_to_kv, tokens=tokens,
                          seq_len=st.seq_len, out=st.scores, hist=st.score_hist)
@@ -609,7 +620,7 @@ def decoder_stage_times(dec, budget, hbm, reps=10):
                                               workspace=st.workspace[i], out=st.out[i])
 
     timed = {}
-    for name in ("score", "score+select", "score+select+attention"):
+    for name in ("score", "score+select", "score+select+attention", "fused", "fused+attention"):
         run(name)
         torch.cuda.synchronize()
         st.score_hist.zero_()
@@ -625,7 +636,11 @@ def decoder_stage_times(dec, budget, hbm, reps=10):
     torch.cuda.synchronize()
     return {"score_ms": timed["score"], "topk_ms": timed["score+select"] - timed["score"],
             "gather_attention_ms": timed["score+select+attention"] - timed["score+select"],
-            "per": f"sparse layer ({len(sparse)} per token); gather is fused into attention"}
+            "score_topk_fused_ms": timed["fused"],
+            "gather_attention_after_fused_ms": timed["fused+attention"] - timed["fused"],
+            "per": f"sparse layer ({len(sparse)} per token); gather is fused into attention; "
+                   "the decode step runs the fused score+topk kernel (score_topk_fused_ms), "
+                   "score_ms/topk_ms are the two-kernel form of the same stage"}
 
 
 def run_reference(args):

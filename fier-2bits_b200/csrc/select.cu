@@ -593,6 +593,7 @@ struct RowShared {
     uint32_t wsum[32];
     uint32_t total;            // this CTA's packed (> thr) << 16 | (== thr), read by peers
     uint32_t sel_bin, sel_above, count;
+    uint32_t sel_count;        // cluster total of the selected bin
     uint32_t base_gt, base_eq;
     uint64_t bar;              // completion of the bulk copy of this CTA's scores
 };
@@ -665,11 +666,11 @@ __device__ void cluster_find_bin(RowShared& sh, int slot, int nbins, uint32_t re
         const uint32_t ab = above1 + s2 - l2;  // count above this lane's bins
         if (lane == 0) {
             sh.count = total;
-            if (!hit) { sh.sel_bin = 0u; sh.sel_above = 0u; }
+            if (!hit) { sh.sel_bin = 0u; sh.sel_above = 0u; sh.sel_count = 0u; }
         }
         if (hit && ab < remaining && ab + l2 >= remaining) {  // exactly one lane
-            if (sub == 2 && ab + c1 >= remaining) { sh.sel_bin = b0 + 1; sh.sel_above = ab; }
-            else { sh.sel_bin = b0; sh.sel_above = ab + (sub == 2 ? c1 : 0u); }
+            if (sub == 2 && ab + c1 >= remaining) { sh.sel_bin = b0 + 1; sh.sel_above = ab; sh.sel_count = c1; }
+            else { sh.sel_bin = b0; sh.sel_above = ab + (sub == 2 ? c1 : 0u); sh.sel_count = sub == 2 ? c0 : l2; }
         }
     }
     __syncthreads();
@@ -936,28 +937,42 @@ __global__ void __launch_bounds__(NT, kRowThreads / NT) select_row_kernel(Select
     const uint32_t d2 = sh.sel_bin;
     prefix |= d2 << 10;
     remaining -= sh.sel_above;
-    // Digit 3 over the keys of the digit-2 bin, visiting only the top-digit bin.
-    uint64_t bin2_bits = 0u;
-    for (uint64_t m = bin_bits; m != 0u; m &= m - 1) {
-        const int j = __ffsll(static_cast<long long>(m)) - 1;
-        const uint32_t x = mine[j];
-        const uint32_t dx = (x >> 10) & 0x7ffu;
-        if (dx > d2) {
-            gt_bits |= 1ull << j;
-        } else if (dx == d2) {
-            bin2_bits |= 1ull << j;
-            atomicAdd(&sh.hist[2][hidx(x & 0x3ffu)], 1u);
-        }
-    }
-    cluster_find_bin<C>(sh, 2, 1024, remaining);
-    const uint32_t thr = prefix | sh.sel_bin;
-    const uint32_t need = remaining - sh.sel_above;
+    // When every key of the digit-2 bin is a pick (the common case: a 22-bit prefix
+    // holds one or two keys), the third digit is not needed: the threshold goes just
+    // below the bin.  The test reads cluster totals, so every CTA takes the same branch.
+    const bool whole_bin = sh.sel_count == remaining && prefix != 0u;
+    uint32_t thr, need;
     uint64_t eq_bits = 0u;
-    for (uint64_t m = bin2_bits; m != 0u; m &= m - 1) {
-        const int j = __ffsll(static_cast<long long>(m)) - 1;
-        const uint32_t x = mine[j];
-        if (x > thr) gt_bits |= 1ull << j;
-        else if (x == thr) eq_bits |= 1ull << j;
+    if (whole_bin) {
+        for (uint64_t m = bin_bits; m != 0u; m &= m - 1) {
+            const int j = __ffsll(static_cast<long long>(m)) - 1;
+            if (((mine[j] >> 10) & 0x7ffu) >= d2) gt_bits |= 1ull << j;
+        }
+        thr = prefix - 1u;
+        need = 0u;
+    } else {
+        // Digit 3 over the keys of the digit-2 bin, visiting only the top-digit bin.
+        uint64_t bin2_bits = 0u;
+        for (uint64_t m = bin_bits; m != 0u; m &= m - 1) {
+            const int j = __ffsll(static_cast<long long>(m)) - 1;
+            const uint32_t x = mine[j];
+            const uint32_t dx = (x >> 10) & 0x7ffu;
+            if (dx > d2) {
+                gt_bits |= 1ull << j;
+            } else if (dx == d2) {
+                bin2_bits |= 1ull << j;
+                atomicAdd(&sh.hist[2][hidx(x & 0x3ffu)], 1u);
+            }
+        }
+        cluster_find_bin<C>(sh, 2, 1024, remaining);
+        thr = prefix | sh.sel_bin;
+        need = remaining - sh.sel_above;
+        for (uint64_t m = bin2_bits; m != 0u; m &= m - 1) {
+            const int j = __ffsll(static_cast<long long>(m)) - 1;
+            const uint32_t x = mine[j];
+            if (x > thr) gt_bits |= 1ull << j;
+            else if (x == thr) eq_bits |= 1ull << j;
+        }
     }
 
     // 4. Rank: (> thr) << 16 | (== thr) counts per thread (slice totals < 2^16), one
