@@ -471,12 +471,24 @@ def run_ours(args):
                          "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": dom["frac"],
                          "traffic": traffic, "algorithmic_bytes": dom["bytes"],
                          "union_rows_per_layer": union_rows},
+            # The fused score + select is bound by the POPC pipe, not by HBM: 24
+            # popcounts per token·query head (5 per head·word + 1 per token·word).
+            "popc_roofline": {
+                "kernel": "score_select",
+                "achieved": B * stack.q_heads * L_now * 24 / (stage_ms.get("score_select", float("nan")) * 1e-3) / 1e9,
+                "peak": 16 * torch.cuda.get_device_properties(dev).multi_processor_count
+                        * float(clocks.summary().get("sm_max_mhz") or 1965.0) / 1e3,
+                "unit": "Gpopc/s", "peak_note": "16 POPC per clock per SM at the max SM clock"}
+            if stack.fused_select else None,
             "clocks": clocks.summary(),
             "e2e": {"value": e2e_layer, "unit": "ms", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": stack.launches_per_step() * args.steps,
             "cpu_baseline": cpu_baseline,
         }
+        if line.get("popc_roofline"):
+            pr = line["popc_roofline"]
+            pr["frac"] = pr["achieved"] / pr["peak"]
         if world > 1:
             line["gather_check"] = gather_check
             line["config"]["gather_wait"] = stack.gather_wait if stack.peer is not None else "nccl"
