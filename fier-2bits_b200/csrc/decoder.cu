@@ -12,6 +12,7 @@
 // (every product and sum of two 16-bit values rounded once), so outputs match
 // them up to the order of the fp32 sum of squares in rmsnorm.
 #include <cmath>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -108,6 +109,88 @@ __global__ void __launch_bounds__(kNormThreads) silu_mul_kernel(const T* __restr
     }
 }
 
+// ------------------------------------------------------------------ GEMV
+// out[j] = round(round(sum_i x[i] * W[j, i]) + residual[j]) for one activation row
+// (batch-1 decode; the product is rounded before the residual add, as
+// `h + o_proj(x)` is): W is [n_out, k] row-major (an nn.Linear weight).  HBM-bound
+// on W.  One 256-thread CTA per kGemvRows rows; warp w takes the w-th eighth of k
+// (split-K), every lane keeps kGemvRows 16-byte weight loads per step in flight,
+// fp32 partial sums meet in shared memory.
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvRows = 4;
+
+template <typename T>
+__device__ __forceinline__ void fma8(float& a, const uint4& wv, const uint4& xv) {
+    const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w}, xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const T* we = reinterpret_cast<const T*>(&wa[j]);
+        const T* xe = reinterpret_cast<const T*>(&xa[j]);
+        a = fmaf(to_float<T>(we[0]), to_float<T>(xe[0]), a);
+        a = fmaf(to_float<T>(we[1]), to_float<T>(xe[1]), a);
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ residual,
+            T* __restrict__ out, int64_t n_out, int k) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float s_part[kGemvWarps][kGemvRows];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kGemvRows;
+    const int chunks = k / 8;
+    const int per_warp = (chunks + kGemvWarps - 1) / kGemvWarps;
+    const int c0 = warp * per_warp;
+    const int c1 = min(chunks, c0 + per_warp);
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const uint4* wr[kGemvRows];
+    float acc[kGemvRows];
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r) {
+        acc[r] = 0.0f;
+        const int64_t row = r0 + r < n_out ? r0 + r : n_out - 1;
+        wr[r] = reinterpret_cast<const uint4*>(w + row * k);
+    }
+    int c = c0 + lane;
+    for (; c + 32 < c1; c += 64) {
+        uint4 wa[kGemvRows], wb[kGemvRows];
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r) {
+            wa[r] = __ldcs(wr[r] + c);
+            wb[r] = __ldcs(wr[r] + c + 32);
+        }
+        const uint4 xa = __ldg(xv + c), xb = __ldg(xv + c + 32);
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r) {
+            fma8<T>(acc[r], wa[r], xa);
+            fma8<T>(acc[r], wb[r], xb);
+        }
+    }
+    if (c < c1) {
+        const uint4 xa = __ldg(xv + c);
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r) fma8<T>(acc[r], __ldcs(wr[r] + c), xa);
+    }
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        if (lane == 0) s_part[warp][r] = acc[r];
+    }
+    __syncthreads();
+    if (threadIdx.x < kGemvRows && r0 + threadIdx.x < n_out) {
+        float v = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kGemvWarps; ++q) v += s_part[q][threadIdx.x];
+        T o = from_float<T>(v);
+        if (residual != nullptr) o = from_float<T>(to_float<T>(o) + to_float<T>(residual[r0 + threadIdx.x]));
+        out[r0 + threadIdx.x] = o;
+    }
+}
+
 }  // namespace
 }  // namespace popkv
 
@@ -191,4 +274,27 @@ extern "C" int popkv_silu_mul(const void* gate_up, void* out, int dtype, int64_t
             return fail(POPKV_ERR_UNSUPPORTED, "silu_mul dtype %d is not fp16/bf16", dtype);
     }
     return check_launch("popkv_silu_mul");
+}
+
+extern "C" int popkv_gemv(const void* x, const void* weight, const void* residual, void* out,
+                          int dtype, int64_t n_out, int64_t k, popkv_stream_t stream) {
+    if (n_out <= 0 || k <= 0) return fail(POPKV_ERR_INVALID_ARGUMENT, "gemv needs n_out > 0 and k > 0");
+    if (k % 8 != 0 || k > (1 << 24)) return fail(POPKV_ERR_UNSUPPORTED, "gemv needs k a multiple of 8");
+    if (!x || !weight || !out) return fail(POPKV_ERR_INVALID_ARGUMENT, "null pointer argument");
+    if (!aligned(x, 16) || !aligned(weight, 16)) return fail(POPKV_ERR_ALIGNMENT, "gemv x and weight need 16-byte alignment");
+    const cudaStream_t st = as_stream(stream);
+    const int64_t grid = (n_out + kGemvRows - 1) / kGemvRows;
+    if (grid > 0x7fffffffLL) return fail(POPKV_ERR_UNSUPPORTED, "gemv: too many rows");
+    auto go = [&](auto kern, auto* tp) {
+        using T = std::remove_pointer_t<decltype(tp)>;
+        launch_pdl(kern, dim3((unsigned)grid), dim3(kGemvThreads), 0, st, static_cast<const T*>(x),
+                   static_cast<const T*>(weight), static_cast<const T*>(residual), static_cast<T*>(out),
+                   n_out, (int)k);
+    };
+    switch (dtype) {
+        case POPKV_BF16: go(gemv_kernel<__nv_bfloat16>, (__nv_bfloat16*)nullptr); break;
+        case POPKV_F16: go(gemv_kernel<__half>, (__half*)nullptr); break;
+        default: return fail(POPKV_ERR_UNSUPPORTED, "gemv dtype %d is not fp16/bf16", dtype);
+    }
+    return check_launch("popkv_gemv");
 }

@@ -484,6 +484,26 @@ void advance(const at::Tensor& seq_len, int64_t increment) {
                  "popkv_advance");
 }
 
+void gemv(const at::Tensor& x, const at::Tensor& weight, const c10::optional<at::Tensor>& residual,
+          const at::Tensor& out) {
+    CHECK_CUDA(x); CHECK_CONTIGUOUS(x); CHECK_CUDA(weight); CHECK_CONTIGUOUS(weight);
+    CHECK_CUDA(out); CHECK_CONTIGUOUS(out);
+    TORCH_CHECK(weight.dim() == 2 && x.numel() == weight.size(1) && out.numel() == weight.size(0),
+                "gemv: x [k], weight [n, k], out [n]");
+    TORCH_CHECK(x.scalar_type() == weight.scalar_type() && out.scalar_type() == x.scalar_type(),
+                "gemv tensors must share a dtype");
+    const void* res = nullptr;
+    if (residual) {
+        CHECK_CUDA(*residual); CHECK_CONTIGUOUS(*residual);
+        TORCH_CHECK(residual->numel() == out.numel() && residual->scalar_type() == x.scalar_type(), "gemv residual");
+        res = residual->data_ptr();
+    }
+    c10::cuda::CUDAGuard guard(x.device());
+    check_status(popkv_gemv(x.data_ptr(), weight.data_ptr(), res, out.data_ptr(), dtype_code(x),
+                            weight.size(0), weight.size(1), stream_of(x)),
+                 "popkv_gemv");
+}
+
 void rmsnorm(const at::Tensor& x, const at::Tensor& weight, double eps, const at::Tensor& out) {
     for (const at::Tensor* t : {&x, &weight, &out}) { CHECK_CUDA((*t)); CHECK_CONTIGUOUS((*t)); }
     TORCH_CHECK(x.scalar_type() == weight.scalar_type() && x.scalar_type() == out.scalar_type(),
@@ -568,6 +588,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("advance", &advance);
     m.def("peer_push", &peer_push);
     m.def("rmsnorm", &rmsnorm);
+    m.def("gemv", &gemv);
     m.def("rope_qkv", &rope_qkv);
     m.def("silu_mul", &silu_mul);
     m.def("version", &popkv_version);

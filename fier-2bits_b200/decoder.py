@@ -16,7 +16,8 @@ Two front ends over the same model (a transformers ``LlamaForCausalLM``):
 
 ``GraphedDecoder``
     Greedy decoding for throughput: the whole token step -- embedding, 32 layers
-    (fused QKV projection, RoPE, retrieval on the kernels, o_proj, MLP), final norm,
+    (fused QKV projection, RoPE, retrieval on the kernels, o_proj, MLP; every weight
+    product a one-row GEMV kernel, popkv_gemv), final norm,
     lm_head and the argmax that feeds the next step -- is one CUDA graph over
     device-resident state (token id, sequence length, K/V caches, packed keys), so
     a step costs one graph launch.  Retrieval and the static-cache append run through
@@ -410,17 +411,17 @@ class GraphedDecoder:
         torch.index_select(self.backbone.embed_tokens.weight, 0, self.token, out=h)
         for i, layer in enumerate(self.backbone.layers):
             pk.rmsnorm(h, layer.input_layernorm.weight, self.eps, self.x)
-            torch.matmul(self.x, self.w_qkv[i].t(), out=self.qkv)
+            pk.gemv(self.x, self.w_qkv[i], self.qkv)
             pk.rope_qkv(self.qkv, self.cos, self.sin, st.seq_len, q_heads=H, kv_heads=KVH,
                         q=st.q_in[i], k=st.k_in[i], v=st.v_in[i])
             st._layer(i, 0)
-            torch.addmm(h, st.out[i].view(1, H * D), layer.self_attn.o_proj.weight.t(), out=self.h2)
+            pk.gemv(st.out[i], layer.self_attn.o_proj.weight, self.h2, residual=h)
             pk.rmsnorm(self.h2, layer.post_attention_layernorm.weight, self.eps, self.x)
-            torch.matmul(self.x, self.w_gate_up[i].t(), out=self.gu)
+            pk.gemv(self.x, self.w_gate_up[i], self.gu)
             pk.silu_mul(self.gu, self.act)
-            torch.addmm(self.h2, self.act, layer.mlp.down_proj.weight.t(), out=h)
+            pk.gemv(self.act, layer.mlp.down_proj.weight, h, residual=self.h2)
         pk.rmsnorm(h, self.backbone.norm.weight, self.eps, self.x)
-        torch.matmul(self.x, self.model.lm_head.weight.t(), out=self.logits_lp)
+        pk.gemv(self.x, self.model.lm_head.weight, self.logits_lp)
         self.logits.copy_(self.logits_lp)
         torch.argmax(self.logits, dim=-1, out=self.token)
         torch.cuda.current_stream().wait_stream(st.side)

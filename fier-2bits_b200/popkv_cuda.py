@@ -288,6 +288,13 @@ def rope_qkv(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, positions:
     extension().rope_qkv(qkv, cos, sin, positions, int(q_heads), int(kv_heads), q, k, v)
 
 
+def gemv(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor,
+         residual: torch.Tensor | None = None) -> torch.Tensor:
+    """out = residual + x @ weight.T for one activation row (fp32 accumulation)."""
+    extension().gemv(x, weight, residual, out)
+    return out
+
+
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """out = round(silu(gate)) * up for gate_up = [gate | up] (LlamaMLP)."""
     extension().silu_mul(gate_up, out)

@@ -318,6 +318,16 @@ int popkv_rope_qkv(const void* qkv, const void* cos_table, const void* sin_table
                    popkv_stream_t stream);
 int popkv_silu_mul(const void* gate_up, void* out, int dtype, int64_t rows, int64_t ffn,
                    popkv_stream_t stream);
+/*
+ * Decoder weight streams (replaces torch.matmul / torch.addmm with one activation
+ * row, the projections of LlamaSparseDecoder.decode, popkv.py:613-616):
+ * out[j] = round(round(sum_i x[i] * weight[j, i]) + residual[j]) (the product rounded
+ * before the residual add, as `h + o_proj(x)`), weight [n_out, k] row-major (an
+ * nn.Linear weight), x [k], residual [n_out] or NULL; fp32 accumulation.
+ * k a multiple of 8; fp16/bf16; x and weight 16-byte aligned.
+ */
+int popkv_gemv(const void* x, const void* weight, const void* residual, void* out, int dtype,
+               int64_t n_out, int64_t k, popkv_stream_t stream);
 
 #ifdef __cplusplus
 }

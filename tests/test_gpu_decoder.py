@@ -131,3 +131,22 @@ def test_fused_decoder_steps_match_transformers_modules():
     pk.silu_mul(gu, act)
     want = torch.nn.functional.silu(gu[:, :512]) * gu[:, 512:]
     assert float((act.float() - want.float()).abs().max()) <= 2 ** -7 * float(want.abs().max())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,k,res", [(6144, 4096, False), (4096, 4096, True), (4096, 14336, True),
+                                     (1000, 72, False), (3, 8, True), (128256, 4096, False)])
+def test_gemv_matches_fp32_matmul(dtype, n, k, res):
+    """popkv_gemv (the decoder's weight products) against an fp32 matmul of the same
+    16-bit inputs: the product rounded once, then the residual added and rounded."""
+    import popkv_cuda as pk
+    g = torch.Generator().manual_seed(n + k)
+    x = torch.randn(k, generator=g).to(dtype).cuda()
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).to(dtype).cuda()
+    r = torch.randn(n, generator=g).to(dtype).cuda() if res else None
+    out = torch.empty(n, dtype=dtype, device="cuda")
+    pk.gemv(x, w, out, residual=r)
+    want = (w.float() @ x.float()).to(dtype).float() + (r.float() if res else 0.0)
+    err = (out.float() - want).abs()
+    tol = 2 ** -7 * want.abs() + 1e-3
+    assert bool((err <= tol).all()), float((err - tol).max())
